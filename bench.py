@@ -1,0 +1,338 @@
+"""Benchmark: attention forward TFLOPS (4*B*H*N^2*d / t) on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 3]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1, one rank per GPU)
+
+Workload (the configuration its 1/2/4/8-GPU metric and
+its 60%-of-peak target are quoted on): B=64 H=64 N=1024 d=64, bf16 Q/K/V ~ N(0,1)
+(seeded, synthetic), scale 1/8, non-causal. The 4096 B*H slices are split over
+the ranks with no collective (strong scaling: total work fixed).
+
+One step = one kernel launch over this rank's slices, inputs resident in HBM.
+`value` = total FLOPs of all ranks / max-over-ranks device time.
+`e2e`   = the same metric through the public API (blackflash_b200.blackflash)
+          with Q/K/V copied from pinned host memory and O copied back each step.
+`--impl reference` times the reference's CPU path (torch fp32 math attention,
+reference tests/test_blackflash.py:16-19) on the host cores, rank 0 only.
+
+Inputs (3 x 512 MiB at N=1) exceed the 126 MB L2, so no flush is needed between
+steps; the JSON says so.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+CONFIGS = {
+    # name: (B, H, N, d, dist)
+    "1": (2, 2, 512, 64, "normal"),
+    "2": (4, 8, 1024, 64, "normal"),
+    "3": (64, 64, 1024, 64, "normal"),
+    "4": (8, 16, 8192, 64, "peaked"),
+}
+METRIC = "attention fwd TFLOPS (4BHN^2d/t)"
+
+# DRAM traffic per launch of the main kernel, from ncu (profiles/fa_fwd_sm100_b64h64n1024.txt):
+# bytes read + written for one full launch of config 3 at N=1. None until measured.
+TRAFFIC_BYTES = {"3": None}
+
+
+def flops(B, H, N, d):
+    return 4.0 * B * H * N * N * d
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"bf16_tflops": p.get("bf16_tflops"), "bf16_tflops_sustained": p.get("bf16_tflops_sustained"),
+                "hbm_gbs": p.get("hbm_gbs"), "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling in the background (200 ms period)."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []  # (host_time, sm_mhz, max_mhz, reasons)
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                sm, mx = float(parts[2]), float(parts[3])
+            except ValueError:
+                continue
+            reasons = [n for n, v in zip(names, parts[6:10]) if v.lower() == "active"]
+            self.samples.append((time.time(), sm, mx, reasons))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0: float, t1: float):
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        window = "timed"
+        if not inside:  # timed region shorter than the sampling period: use the loaded samples around it
+            inside = [s for s in self.samples if t0 - 1.0 <= s[0] <= t1 + 0.5]
+            window = "timed+-1s"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "window": "none"}
+        reasons = sorted({r for s in inside for r in s[3]})
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": max(s[2] for s in inside),
+                "reasons": reasons, "samples": len(inside), "window": window}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_reference_sample(B, H, N, d, dist, budget_s: float, seed: int = 0):
+    """Reference CPU path (torch fp32 math, tests/test_blackflash.py:16-19) on a bounded
+    sample of the workload's slices; returns (TFLOPS, slices, seconds, threads)."""
+    from blackflash_b200.inputs import make_qkv
+    from oracle import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    chunk = 4
+    q, k, v = make_qkv(1, chunk, N, d, dist=dist, seed=seed)
+    oracle.torch_math(q, k, v, 1.0 / math.sqrt(d))  # warm-up
+    done, t0 = 0, time.perf_counter()
+    while True:
+        oracle.torch_math(q, k, v, 1.0 / math.sqrt(d))
+        done += chunk
+        el = time.perf_counter() - t0
+        if el >= budget_s or done >= B * H:
+            break
+    return flops(1, done, N, d) / el / 1e12, done, el, torch.get_num_threads()
+
+
+def run_reference(args, cfg_name):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return  # rank 0 alone runs the CPU reference
+    B, H, N, d, dist = CONFIGS[cfg_name]
+    per_step = []
+    for _ in range(args.warmup):
+        cpu_reference_sample(B, H, N, d, dist, budget_s=0.5)
+    slices = 0
+    threads = 1
+    for _ in range(args.steps):
+        tf, n_sl, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.ref_step_seconds)
+        per_step.append(tf)
+        slices = n_sl
+    value = statistics.mean(per_step)
+    sample = f"{slices} of {B*H} (b,h) slices per step, N={N}, torch fp32 CPU math; TFLOPS scaled per slice"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": flops(B, H, N, d) / (value * 1e12) * 1e3 if value > 0 else None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal", "global_batch": B, "seq_len": N,
+                   "parallelism": "cpu host cores (rank 0 only)"},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, cfg_name):
+    import torch.distributed as dist_mod
+
+    from blackflash_b200 import _lib, blackflash
+    from blackflash_b200.inputs import make_qkv
+    from blackflash_b200.shard import slice_range
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist_mod.init_process_group("nccl", device_id=dev)
+
+    B, H, N, d, dist = CONFIGS[cfg_name]
+    total = B * H
+    s0, s1 = slice_range(total, world, rank)
+    my = s1 - s0
+    q, k, v = make_qkv(1, my, N, d, dist=dist, seed=1000 + rank, device=dev)
+    O = torch.empty_like(q)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+    scale = 1.0 / math.sqrt(d)
+
+    def step():
+        rc = lib.blackflash_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), O.data_ptr(), None, None, 1, my, N, d,
+                                scale, stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(lib.blackflash_last_error().decode())
+
+    def barrier():
+        if world > 1:
+            dist_mod.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist_mod.all_reduce(t, op=dist_mod.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    # keep the GPU loaded while the sampler settles
+    for _ in range(max(1, args.warmup)):
+        step()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    h1 = time.time()
+    barrier()
+    ms_local = ev0.elapsed_time(ev1)
+    sampler.stop()
+    ms_total = max_over_ranks(ms_local)
+    ms_step = ms_total / args.steps
+    f_total = flops(B, H, N, d)
+    f_rank = flops(1, my, N, d)
+    value = f_total / (ms_step * 1e-3) / 1e12
+    clocks = sampler.summary(h0, h1)
+
+    # ---- end to end through the public API, host buffers (pinned) in and out
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    oh = torch.empty(O.shape, dtype=O.dtype, pin_memory=True)
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+
+    def e2e_step():
+        qd = qh.to(dev, non_blocking=True)
+        kd = kh.to(dev, non_blocking=True)
+        vd = vh.to(dev, non_blocking=True)
+        od = blackflash(qd, kd, vd, scale)
+        oh.copy_(od, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+    e2e_value = f_total / (e2e_ms * 1e-3) / 1e12
+    bytes_in = 3 * q.numel() * q.element_size()
+    bytes_out = O.numel() * O.element_size()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, n_sl, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.cpu_seconds)
+        cpu = {"value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",
+               "sample": f"{n_sl} of {total} (b,h) slices of the same workload, torch fp32 CPU math "
+                         f"(reference tests/test_blackflash.py:16-19), {el:.1f} s"}
+
+    if rank == 0:
+        peaks = load_peaks()
+        per_gpu_achieved = f_rank / (ms_local / args.steps * 1e-3) / 1e12  # rank 0's kernel rate
+        peak = peaks["bf16_tflops"]
+        traffic = TRAFFIC_BYTES.get(cfg_name)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal, scale 1/8",
+                       "global_batch": B, "seq_len": N, "parallelism": f"bxh{world} (no collective)",
+                       "l2": "inputs larger than L2 (no flush)", "slices_per_rank": my},
+            "roofline": {"bound": "tensor", "achieved": per_gpu_achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": per_gpu_achieved / peak if peak else None, "traffic": traffic,
+                         "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
+                         "kernel": "fa_fwd_sm100_kernel", "flops_per_launch": f_rank},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": bytes_in,
+                    "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms},
+            "gpu_launches": args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist_mod.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="3")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=2.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args, args.config)
+    else:
+        run_ours(args, args.config)
+
+
+if __name__ == "__main__":
+    main()

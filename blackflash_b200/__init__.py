@@ -1,0 +1,14 @@
+"""BlackFlash-B200: a B200-native (sm_100a) attention forward behind BlackFlash's API.
+
+    from blackflash_b200 import blackflash
+    O = blackflash(Q, K, V)            # Q, K, V: [B, H, N, 64] bf16 CUDA
+
+The compute path is libblackflash_b200.so (tcgen05 / TMA / TMEM kernel); there
+is no CPU fallback.
+"""
+from .ops import (attention_partial, blackflash, forward, forward_lse, lse_merge_,  # noqa: F401
+                  to_bf16, wait_status)
+from . import blackflash_cuda  # noqa: F401
+
+__all__ = ["blackflash", "forward", "forward_lse", "attention_partial", "lse_merge_", "to_bf16", "wait_status",
+           "blackflash_cuda"]

@@ -1,0 +1,27 @@
+// Internal launch descriptor shared by the C-ABI wrappers and the kernel file.
+#pragma once
+#include <stdint.h>
+
+#include "../../include/blackflash_b200.h"
+
+struct BfFwdArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* o;          // bf16 [BH, n_q, 64] or null when o_f32 is set
+    float* o_f32;     // fp32 [BH, n_q, 64] partial-mode output, or null
+    float* lse;       // [BH, n_q] or null
+    float* row_max;   // [BH, n_q] or null
+    long long bh;
+    int n_q;
+    int n_kv;
+    int d;
+    float scale;
+    void* stream;
+    unsigned long long timeout_ns;  // 0 = default
+    float* dbg_s;
+    int skip_k_loads;
+};
+
+int bf_fwd_launch(const BfFwdArgs* a);
+int bf_set_error(int code, const char* msg);

@@ -1,0 +1,133 @@
+"""Torch-facing operators over the C ABI.
+
+`forward` mirrors the reference's torch extension function
+`blackflash_cuda.forward` (binding/blackflash_ops.cu:18-55): same argument
+order and meaning, same checks (CUDA, bf16, contiguous, d == 64), the same
+RuntimeError on a failed check, and a fresh bf16 O as the result. What differs:
+  * it launches on Q's device (the reference has no device guard and uses
+    whatever device is current);
+  * it does not allocate and fill the unused l/m buffers on every call;
+  * K and V must have Q's shape (the reference reads them with Q's sizes
+    without checking).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_qkv(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor) -> None:
+    for name, t in (("Q", Q), ("K", K), ("V", V)):
+        _require(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
+        _require(t.is_cuda and t.dtype == torch.bfloat16, f"{name} must be a CUDA bfloat16 tensor")
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+        _require(t.dim() == 4, f"{name} must be [B, H, N, d]")
+    _require(K.shape == Q.shape and V.shape == Q.shape, "Q, K and V must have the same shape")
+    _require(K.device == Q.device and V.device == Q.device, "Q, K and V must be on the same device")
+    _require(Q.size(3) == 64, "BlackFlash currently only supports d=64")
+
+
+def _stream_handle(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float) -> torch.Tensor:
+    """O = softmax(scale * Q K^T) V; bf16 [B, H, N, 64] in and out."""
+    return forward_lse(Q, K, V, scale, want_stats=False)[0]
+
+
+def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float, want_stats: bool = True):
+    """Like `forward`, and also returns (lse, row_max), each fp32 [B, H, N].
+
+    lse[b,h,i] = log sum_j exp(scale * S_ij) and row_max[b,h,i] = max_j scale * S_ij:
+    the two quantities the reference's l/m slots were declared for
+    (include/flash_attn.cuh:27-28).
+    """
+    _check_qkv(Q, K, V)
+    B, H, N, d = Q.shape
+    O = torch.empty_like(Q)
+    lse = m = None
+    if want_stats:
+        lse = torch.empty((B, H, N), dtype=torch.float32, device=Q.device)
+        m = torch.empty((B, H, N), dtype=torch.float32, device=Q.device)
+    if Q.numel() == 0:
+        return O, lse, m
+    lib = _lib.load()
+    with torch.cuda.device(Q.device):
+        rc = lib.blackflash_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                                lse.data_ptr() if lse is not None else None,
+                                m.data_ptr() if m is not None else None,
+                                B, H, N, d, float(scale), _stream_handle(Q.device))
+    _lib.check(rc, "blackflash_fwd")
+    return O, lse, m
+
+
+def blackflash(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+    """Attention forward. Mirrors the reference's Python API (blackflash/__init__.py:5-18):
+    Q, K, V are [B, H, N, d] bf16 CUDA tensors with d == 64; scale defaults to 1/sqrt(d)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(Q.size(-1))
+    return forward(Q, K, V, scale)
+
+
+def attention_partial(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float):
+    """One ring step: Q [S, Nq, 64] against K/V [S, Nkv, 64] (S = flattened slices).
+
+    Returns (O_f32 [S, Nq, 64] normalised over this KV block, lse [S, Nq])."""
+    for name, t in (("Q", Q), ("K", K), ("V", V)):
+        _require(t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.dim() == 3,
+                 f"{name} must be a contiguous CUDA bf16 [slices, rows, 64] tensor")
+    _require(Q.size(0) == K.size(0) == V.size(0) and K.shape == V.shape and Q.size(2) == 64 and K.size(2) == 64,
+             "partial attention needs Q [S,Nq,64] and K,V [S,Nkv,64]")
+    S, Nq, _ = Q.shape
+    Nkv = K.size(1)
+    O = torch.empty((S, Nq, 64), dtype=torch.float32, device=Q.device)
+    lse = torch.empty((S, Nq), dtype=torch.float32, device=Q.device)
+    lib = _lib.load()
+    with torch.cuda.device(Q.device):
+        rc = lib.blackflash_fwd_partial(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), lse.data_ptr(),
+                                        S, Nq, Nkv, 64, float(scale), _stream_handle(Q.device))
+    _lib.check(rc, "blackflash_fwd_partial")
+    return O, lse
+
+
+def lse_merge_(O_acc: torch.Tensor, lse_acc: torch.Tensor, O_part: torch.Tensor, lse_part: torch.Tensor) -> None:
+    """In-place log-sum-exp merge of a partial result into the running one (fp32)."""
+    for t in (O_acc, lse_acc, O_part, lse_part):
+        _require(t.is_cuda and t.dtype == torch.float32 and t.is_contiguous(), "merge operands must be contiguous CUDA fp32")
+    rows = lse_acc.numel()
+    _require(O_acc.numel() == rows * 64 and O_part.numel() == rows * 64 and lse_part.numel() == rows,
+             "merge operands disagree in size")
+    lib = _lib.load()
+    with torch.cuda.device(O_acc.device):
+        rc = lib.blackflash_lse_merge(O_acc.data_ptr(), lse_acc.data_ptr(), O_part.data_ptr(), lse_part.data_ptr(),
+                                      rows, 64, _stream_handle(O_acc.device))
+    _lib.check(rc, "blackflash_lse_merge")
+
+
+def to_bf16(src: torch.Tensor) -> torch.Tensor:
+    """fp32 -> bf16 through the library's cast kernel."""
+    _require(src.is_cuda and src.dtype == torch.float32 and src.is_contiguous(), "src must be contiguous CUDA fp32")
+    dst = torch.empty(src.shape, dtype=torch.bfloat16, device=src.device)
+    if src.numel():
+        lib = _lib.load()
+        with torch.cuda.device(src.device):
+            rc = lib.blackflash_f32_to_bf16(src.data_ptr(), dst.data_ptr(), src.numel(), _stream_handle(src.device))
+        _lib.check(rc, "blackflash_f32_to_bf16")
+    return dst
+
+
+def wait_status(reset: bool = True) -> int:
+    """Device-side wait-timeout status of the current device (0 = none). Synchronous."""
+    import ctypes
+    out = ctypes.c_uint(0)
+    _lib.check(_lib.load().blackflash_status(1 if reset else 0, ctypes.byref(out)), "blackflash_status")
+    return int(out.value)

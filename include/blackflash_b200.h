@@ -1,0 +1,98 @@
+/*
+ * BlackFlash-B200 C ABI: attention forward (non-causal, bf16, head dim 64) on
+ * sm_100a.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed
+ * as `void*`. Calls are asynchronous on that stream. They return BF_OK or an
+ * error code, and blackflash_last_error() gives the message for the calling
+ * thread. No entry point allocates device memory or synchronises the device,
+ * except the ones documented as synchronous (blackflash_status).
+ *
+ * Layouts: Q, K, V and O are contiguous [B, H, N, 64] bf16 (the same layout as
+ * the reference, binding/blackflash_ops.cu:24-27). lse and row_max are [B, H, N]
+ * fp32.
+ */
+#ifndef BLACKFLASH_B200_H
+#define BLACKFLASH_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BF_OK 0
+#define BF_ERR_ARG 1     /* bad shape, pointer or alignment */
+#define BF_ERR_CUDA 2    /* a CUDA runtime/driver call failed */
+#define BF_ERR_TIMEOUT 3 /* a device-side wait exceeded its limit (see blackflash_status) */
+
+/*
+ * O = softmax(scale * Q K^T) V for every (b, h) slice.
+ *
+ * Replaces flash_attn_naive_launch (reference include/flash_attn.cuh:22-32,
+ * kernel/flash_attn_mma.cu:470-518). The arguments mean the same, with three
+ * differences: it returns a status instead of calling exit(), it takes the
+ * stream as void*, and it fills `lse` / `row_max` when they are non-null.
+ * The reference documents those two slots but never writes them.
+ *   lse[b,h,i]     = log(sum_j exp(scale * S_ij))   (natural log)
+ *   row_max[b,h,i] = max_j scale * S_ij
+ * Requirements: d == 64, B, H, N >= 1, every pointer 16-byte aligned.
+ * N need not be a multiple of 128: the kernel masks the ragged KV tile and
+ * skips stores past row N.
+ */
+int blackflash_fwd(const void* Q, const void* K, const void* V, void* O, float* lse, float* row_max, int B, int H,
+                   int N, int d, float scale, void* stream);
+
+/*
+ * Partial attention of one query block against one KV block. It is the
+ * per-step kernel of the ring (sequence-parallel) mode and has no counterpart
+ * in the reference.
+ *   Q: [BH, Nq, 64] bf16; K, V: [BH, Nkv, 64] bf16
+ *   O_f32: [BH, Nq, 64] fp32, normalised over this KV block only
+ *   lse:   [BH, Nq] fp32 logsumexp over this KV block (required)
+ */
+int blackflash_fwd_partial(const void* Q, const void* K, const void* V, float* O_f32, float* lse, long long BH,
+                           int Nq, int Nkv, int d, float scale, void* stream);
+
+/*
+ * Log-sum-exp merge of one partial result into a running one, in place:
+ *   lse' = log(exp(lse_acc) + exp(lse_part))
+ *   O'   = O_acc * exp(lse_acc - lse') + O_part * exp(lse_part - lse')
+ * rows = BH * Nq. A row whose lse_acc is -inf takes the partial unchanged.
+ */
+int blackflash_lse_merge(float* O_acc, float* lse_acc, const float* O_part, const float* lse_part, long long rows,
+                         int d, void* stream);
+
+/* fp32 -> bf16 (round to nearest even), n elements. */
+int blackflash_f32_to_bf16(const float* src, void* dst, long long n, void* stream);
+
+/*
+ * Wait-timeout status of the current device. It is synchronous: it reads a
+ * device word that a kernel sets when one of its bounded mbarrier waits gives
+ * up. *out receives 0 if no wait gave up, otherwise the code of the first wait
+ * site that did. With reset != 0 the word is cleared after it is read.
+ */
+int blackflash_status(int reset, unsigned* out);
+
+/*
+ * Test hook: the same launch as blackflash_fwd, except that the producer never
+ * issues the K loads. The consumers' bounded waits therefore run out after
+ * timeout_ns, the kernel returns early, and blackflash_status reports the
+ * site. No fault or hang is involved. O is left undefined.
+ */
+int blackflash_fwd_timeout_probe(const void* Q, const void* K, const void* V, void* O, int B, int H, int N, int d,
+                                 float scale, unsigned long long timeout_ns, void* stream);
+
+/* Test hook: raw fp32 S = Q K^T of the first 128x128 tile (CTA 0), written to dbg_s. */
+int blackflash_fwd_debug_s(const void* Q, const void* K, const void* V, void* O, float* dbg_s, int B, int H, int N,
+                           int d, float scale, void* stream);
+
+/* Message for the last error returned on this thread ("" if none). */
+const char* blackflash_last_error(void);
+
+/* ABI version of this library (incremented on any signature change). */
+int blackflash_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BLACKFLASH_B200_H */

@@ -42,6 +42,8 @@ CONFIGS = {
     "2": (4, 8, 1024, 64, "normal"),
     "3": (64, 64, 1024, 64, "normal"),
     "4": (8, 16, 8192, 64, "peaked"),
+    # profiling case: same per-slice shape as config 3, 1/4 of the slices (1.6 GB device memory)
+    "prof": (16, 64, 1024, 64, "normal"),
 }
 METRIC = "attention fwd TFLOPS (4BHN^2d/t)"
 

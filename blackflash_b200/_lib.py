@@ -22,6 +22,7 @@ EXPORTED = (
     "blackflash_status",
     "blackflash_fwd_timeout_probe",
     "blackflash_fwd_debug_s",
+    "blackflash_fwd_trace",
     "blackflash_last_error",
     "blackflash_abi_version",
 )
@@ -39,6 +40,7 @@ _SIGS = {
     "blackflash_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
     "blackflash_fwd_timeout_probe": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, ctypes.c_ulonglong, _vp]),
     "blackflash_fwd_debug_s": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp]),
+    "blackflash_fwd_trace": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp]),
     "blackflash_last_error": (ctypes.c_char_p, []),
     "blackflash_abi_version": (_i, []),
 }

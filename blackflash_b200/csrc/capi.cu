@@ -94,6 +94,18 @@ extern "C" int blackflash_fwd_debug_s(const void* Q, const void* K, const void* 
     return bf_fwd_launch(&a);
 }
 
+extern "C" int blackflash_fwd_trace(const void* Q, const void* K, const void* V, void* O, long long* trace,
+                                    int trace_cta, int B, int H, int N, int d, float scale, void* stream) {
+    g_last_error[0] = 0;
+    if (check_bhn(B, H, N) != BF_OK) return BF_ERR_ARG;
+    if (!trace) return bf_set_error(BF_ERR_ARG, "trace buffer required");
+    BfFwdArgs a = base_args(Q, K, V, B, H, N, d, scale, stream);
+    a.o = O;
+    a.trace = trace;
+    a.trace_cta = trace_cta;
+    return bf_fwd_launch(&a);
+}
+
 // Reference-signature launcher (include/flash_attn.cuh:22-32 of the reference).
 void flash_attn_naive_launch(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
                              __nv_bfloat16* O, float* l, float* m, int B, int H, int N, int d, float scale,

@@ -6,24 +6,33 @@
 // fp32 accumulation. The reference's row-max / logsumexp slots
 // (include/flash_attn.cuh:27-28, never written there) are filled here.
 //
-// Structure of one CTA (384 threads, one CTA per SM):
-//   * two 128-row query tiles of one (b, h) slice -> 256 query rows;
+// Persistent kernel: one CTA per SM (384 threads) walks work items
+// item = blockIdx.x + k * gridDim.x; an item is two 128-row query tiles
+// (256 rows) of one (b, h) slice against all of its KV rows. Roles:
 //   * warps 0-3 / 4-7: softmax warpgroups for query tile 0 / 1. One thread
 //     owns one query row (= one TMEM lane), so row max / row sum need no
 //     shuffles. They also rescale O in TMEM (lazily) and run the epilogue;
-//   * warp 8: TMA producer (Q once; K and V per 128-row KV tile into a
-//     STAGES-deep mbarrier ring, 128-byte swizzle);
+//   * warp 8: TMA producer: Q (double-buffered across items) and K / V per
+//     128-row KV tile into a kStages-deep mbarrier ring, 128-byte swizzle;
 //   * warp 9: allocates TMEM and issues every tcgen05.mma:
 //       S_t = Q_t K_j^T   (M=128, N=128, K=64; A,B from smem)      -> TMEM
 //       O_t += P_t V_j    (M=128, N=64,  K=128; A=P from TMEM, B=V) -> TMEM
-//     P_t is written by the softmax threads as bf16 over the first 64
-//     columns of S_t, so P never leaves the SM.
-// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384).
+//     P_t is written by the softmax threads as bf16 into its own TMEM
+//     columns, so P never leaves the SM.
+// TMEM columns (all 512): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
+//                         O0 [384,448) O1 [448,512).
 //
-// MMA issue order per KV tile j: PV0(j-1), S0(j), PV1(j-1), S1(j). Because
-// tcgen05 ops from one thread complete in order and the commit that signals
-// "S_t(j) ready" is issued after PV_t(j-1), a softmax warpgroup that has
-// observed S_t(j) may read/rescale O_t without racing the tensor core.
+// Pipelining. The MMA issuer walks one flat stream of KV steps across work
+// items: S(g) for both tiles, then PV(g-1) for both tiles. A softmax
+// warpgroup releases S_t (s_empty) as soon as S_t(g) is in registers, so the
+// tensor core computes S_t(g+1) - possibly the next item's - while the
+// exponentials of step g run; it waits for PV_t(g-1) (pv_done) only before it
+// overwrites P_t or touches O_t. The next item's Q / K / V are in flight
+// while the current item's last steps and epilogue run.
+//
+// Exponentials: p = 2^(s * scale * log2 e - m). Most run on MUFU (ex2); a fixed
+// share (kEmuPairs of 8 pairs) runs on the FMA pipe (exp2_poly_x2) so both
+// pipes share the load. Arithmetic on pairs uses the sm_100 f32x2 forms.
 //
 // Every mbarrier wait is bounded (WaitCtl): a lost arrival sets a status
 // word and the kernel unwinds instead of spinning forever.
@@ -43,27 +52,34 @@ __device__ unsigned int g_wait_status = 0;
 constexpr int kD = 64;          // head dimension
 constexpr int kBM = 128;        // query rows per tile
 constexpr int kBN = 128;        // KV rows per tile
-constexpr int kQTiles = 2;      // query tiles per CTA
+constexpr int kQTiles = 2;      // query tiles per work item
 constexpr int kStages = 3;      // K/V ring depth
 constexpr int kThreads = 384;
-constexpr int kTileBytes = kBM * kD * 2;  // 16 KiB (Q, K or V tile, bf16)
+constexpr int kTileBytes = kBM * kD * 2;  // 16 KiB (Q, K, V or O tile, bf16)
 constexpr int kTmemCols = 512;
+#ifndef BF_EMU_PAIRS
+#define BF_EMU_PAIRS 2
+#endif
+constexpr int kEmuPairs = BF_EMU_PAIRS;  // of every 8 exp2 pairs, how many run on the FMA pipe
 
 // Shared-memory layout, offsets from a 1024-byte aligned base.
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQTiles * kTileBytes;
-constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffBar = kOffV + kStages * kTileBytes;
+constexpr int kOffQ = 0;                                  // [2 buffers][2 tiles]
+constexpr int kOffK = kOffQ + 2 * kQTiles * kTileBytes;   // [kStages]
+constexpr int kOffV = kOffK + kStages * kTileBytes;       // [kStages]
+constexpr int kOffO = kOffV + kStages * kTileBytes;       // [2 tiles] bf16 output staging
+constexpr int kOffBar = kOffO + kQTiles * kTileBytes;
 
 struct Bars {
-    uint64_t q_full;
+    uint64_t q_full[2];
+    uint64_t q_empty[2];
     uint64_t k_full[kStages];
     uint64_t k_empty[kStages];
     uint64_t v_full[kStages];
     uint64_t v_empty[kStages];
     uint64_t s_full[kQTiles];
+    uint64_t s_empty[kQTiles];
     uint64_t p_full[kQTiles];
-    uint64_t o_full[kQTiles];
+    uint64_t pv_done[kQTiles];
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
@@ -73,35 +89,52 @@ constexpr int kSmemBytes = kOffBar + (int)sizeof(Bars) + 1024;  // + alignment s
 
 // Status codes written by a bounded wait that gave up (first one wins).
 enum : unsigned {
+    kSiteProdQEmpty = 0x100,
     kSiteProdKEmpty = 0x101,
     kSiteProdVEmpty = 0x102,
     kSiteMmaQ = 0x201,
     kSiteMmaK = 0x202,
     kSiteMmaV = 0x203,
     kSiteMmaP = 0x204,
+    kSiteMmaSEmpty = 0x205,
     kSiteSoftS = 0x301,
     kSiteSoftO = 0x302,
+    kSiteSoftPV = 0x303,
 };
 
 struct KParams {
     int n_q;        // query rows per slice
     int n_kv;       // key/value rows per slice
     int q_blocks;   // ceil(n_q / 256)
+    int items;      // bh * q_blocks
     float scale_log2;  // scale * log2(e)
     float scale;
     float* lse;     // [BH, n_q] natural-log logsumexp of scale*S, optional
     float* row_max; // [BH, n_q] max_j scale*S_ij, optional
     float* o_f32;   // [BH, n_q, 64] fp32 normalised output (partial mode), else null
     unsigned long long timeout_ns;
-    float* dbg_s;   // optional: raw S of (CTA 0, tile 0, KV tile 0), 128x128 fp32
+    float* dbg_s;   // optional: raw S of (item 0, tile 0, KV tile 0), 128x128 fp32
     int skip_k_loads;  // test hook: producer never loads K (forces a wait timeout)
+    long long* trace;  // kTrace builds: clock64 event stamps of CTA `trace_cta`
+    int trace_cta;
 };
+
+// Pipeline event trace (diagnostic builds only): trace[role * 512 + g * 8 + ev]
+// holds clock64() - t0 of CTA p.trace_cta for its first 64 global KV steps.
+// Roles: 0/1 softmax warpgroup 0/1 (lane 0 of its first warp), 2 MMA issuer,
+// 3 TMA producer.
+#define BF_TRACE(role, g, ev)                                                                       \
+    do {                                                                                            \
+        if constexpr (kTrace) {                                                                     \
+            if (tracing && (g) < 64) p.trace[(role) * 512 + (g) * 8 + (ev)] = clock64() - trace_t0; \
+        }                                                                                           \
+    } while (0)
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-template <bool kF32Out>
+template <bool kF32Out, bool kTrace = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -112,12 +145,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int bh = blockIdx.x / p.q_blocks;
-    const int q_row0 = (blockIdx.x % p.q_blocks) * (kQTiles * kBM);
     const int nk = (p.n_kv + kBN - 1) / kBN;
+    const long long trace_t0 = kTrace ? clock64() : 0;
+    const bool trace_hit = kTrace && (int)blockIdx.x == p.trace_cta;
 
     if (threadIdx.x == 0) {
-        mbar_init(smem_addr(&bars->q_full), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_addr(&bars->q_full[b]), 1);
+            mbar_init(smem_addr(&bars->q_empty[b]), 1);
+        }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(smem_addr(&bars->k_full[s]), 1);
             mbar_init(smem_addr(&bars->k_empty[s]), 1);
@@ -126,8 +162,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int t = 0; t < kQTiles; ++t) {
             mbar_init(smem_addr(&bars->s_full[t]), 1);
+            mbar_init(smem_addr(&bars->s_empty[t]), kBM);
             mbar_init(smem_addr(&bars->p_full[t]), kBM);
-            mbar_init(smem_addr(&bars->o_full[t]), 1);
+            mbar_init(smem_addr(&bars->pv_done[t]), 1);
         }
         mbar_init(smem_addr(&bars->drain), 1);
         bars->abort_flag = 0;
@@ -163,97 +200,141 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tS = tmem + lane_off + (uint32_t)(t * kBN);
-        const uint32_t tO = tmem + lane_off + (uint32_t)(2 * kBN + t * kD);
+        const uint32_t tP = tmem + lane_off + (uint32_t)(2 * kBN + t * kD);
+        const uint32_t tO = tmem + lane_off + (uint32_t)(2 * kBN + 2 * kD + t * kD);
         const float sl2 = p.scale_log2;
+        const uint64_t sl2_2 = f2_pack(sl2, sl2);
         const uint32_t bar_s = smem_addr(&bars->s_full[t]);
+        const uint32_t bar_se = smem_addr(&bars->s_empty[t]);
         const uint32_t bar_p = smem_addr(&bars->p_full[t]);
-
-        float m_use = -INFINITY;  // reference max (log2 domain) the current P/O/l are relative to
-        float m_raw = -INFINITY;  // true running max of raw scores
-        float l_sum = 0.f;
+        const uint32_t bar_pv = smem_addr(&bars->pv_done[t]);
+        const bool issuer = (warp & 3) == 0 && lane == 0;  // issues this warpgroup's TMA stores
+        const bool tracing = trace_hit && issuer;
+        uint8_t* stage = smem + kOffO + t * kTileBytes;
+        uint32_t g = 0;  // global KV step of this CTA
         bool ok = true;
 
-        for (int j = 0; j < nk; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(bar_s, (uint32_t)(j & 1), ctl, kSiteSoftS));
+        for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+            const int bh = item / p.q_blocks;
+            const int q_row0 = (item % p.q_blocks) * (kQTiles * kBM);
+            float m_use = -INFINITY;  // reference max (log2 domain) the current P/O/l are relative to
+            float m_raw = -INFINITY;  // true running max of raw scores
+            float l_sum = 0.f;
+
+            for (int j = 0; j < nk; ++j, ++g) {
+                BF_TRACE(t, g, 0);
+                if (!(ok = warp_wait(bar_s, g & 1u, ctl, kSiteSoftS))) break;
+                tc_fence_after();
+                BF_TRACE(t, g, 1);
+
+                uint32_t s[4][32];
+                tmem_ld32(tS + 0, s[0]);
+                tmem_ld32(tS + 32, s[1]);
+                tmem_ld32(tS + 64, s[2]);
+                tmem_ld32(tS + 96, s[3]);
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(bar_se);  // S_t may now be overwritten by the next step's S_t
+                BF_TRACE(t, g, 2);
+
+                if (p.dbg_s != nullptr && item == 0 && t == 0 && j == 0) {
+#pragma unroll
+                    for (int c = 0; c < kBN; ++c) p.dbg_s[row * kBN + c] = __uint_as_float(s[c >> 5][c & 31]);
+                }
+
+                const int valid = p.n_kv - j * kBN;  // >= 1
+                if (valid < kBN) {
+#pragma unroll
+                    for (int c = 0; c < kBN; ++c)
+                        if (c >= valid) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+                }
+
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 32; c += 2) {
+                    mx0 = fmax3(mx0, __uint_as_float(s[0][c]), __uint_as_float(s[0][c + 1]));
+                    mx1 = fmax3(mx1, __uint_as_float(s[1][c]), __uint_as_float(s[1][c + 1]));
+                    mx2 = fmax3(mx2, __uint_as_float(s[2][c]), __uint_as_float(s[2][c + 1]));
+                    mx3 = fmax3(mx3, __uint_as_float(s[3][c]), __uint_as_float(s[3][c + 1]));
+                }
+                const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+                m_raw = fmaxf(m_raw, mx);
+                const float m_new = mx * sl2;
+                BF_TRACE(t, g, 3);
+
+                // Lazy rescale: keep the old reference max unless the tile max exceeds
+                // it by more than 8 (log2 units), i.e. P entries stay <= 256.
+                const bool need = m_new > m_use + 8.0f;
+                float alpha = 1.f;
+                if (need) {
+                    alpha = fast_exp2(m_use - m_new);  // 0 on the first tile
+                    m_use = m_new;
+                }
+                l_sum *= alpha;
+
+                const uint64_t negm_2 = f2_pack(-m_use, -m_use);
+                uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = f2_pack(0.f, 0.f);
+                uint32_t pk[4][16];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const uint64_t x2 = f2_fma(
+                            f2_pack(__uint_as_float(s[q][2 * c]), __uint_as_float(s[q][2 * c + 1])), sl2_2, negm_2);
+                        uint64_t p2;
+                        if ((c & 7) < kEmuPairs) {
+                            p2 = exp2_poly_x2(x2);
+                        } else {
+                            float x0, x1;
+                            f2_unpack(x2, x0, x1);
+                            p2 = f2_pack(fast_exp2(x0), fast_exp2(x1));
+                        }
+                        if (c & 1)
+                            sum_b = f2_add(sum_b, p2);
+                        else
+                            sum_a = f2_add(sum_a, p2);
+                        float p0, p1;
+                        f2_unpack(p2, p0, p1);
+                        pk[q][c] = pack_bf16x2(p0, p1);
+                    }
+                }
+                {
+                    float a0, a1, b0, b1;
+                    f2_unpack(sum_a, a0, a1);
+                    f2_unpack(sum_b, b0, b1);
+                    l_sum += (a0 + a1) + (b0 + b1);
+                }
+                BF_TRACE(t, g, 4);
+
+                // P_t of the previous step must have been consumed (and O_t be final)
+                // before we overwrite P_t / rescale O_t.
+                if (g > 0) {
+                    if (!(ok = warp_wait(bar_pv, (g - 1) & 1u, ctl, kSiteSoftPV))) break;
+                    tc_fence_after();
+                }
+                BF_TRACE(t, g, 5);
+                if (j > 0 && __any_sync(0xffffffffu, need)) {
+                    uint32_t o[32];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        tmem_ld32(tO + h * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                        tmem_st32(tO + h * 32, o);
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) tmem_st16(tP + q * 16, pk[q]);
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(bar_p);
+                BF_TRACE(t, g, 6);
+            }
             if (!ok) break;
-            tc_fence_after();
 
-            uint32_t s[4][32];
-            tmem_ld32(tS + 0, s[0]);
-            tmem_ld32(tS + 32, s[1]);
-            tmem_ld32(tS + 64, s[2]);
-            tmem_ld32(tS + 96, s[3]);
-            tmem_wait_ld();
-
-            if (p.dbg_s != nullptr && blockIdx.x == 0 && t == 0 && j == 0) {
-#pragma unroll
-                for (int c = 0; c < kBN; ++c) p.dbg_s[row * kBN + c] = __uint_as_float(s[c >> 5][c & 31]);
-            }
-
-            const int valid = p.n_kv - j * kBN;  // >= 1
-            if (valid < kBN) {
-#pragma unroll
-                for (int c = 0; c < kBN; ++c)
-                    if (c >= valid) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
-            }
-
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                mx0 = fmaxf(mx0, __uint_as_float(s[0][c]));
-                mx1 = fmaxf(mx1, __uint_as_float(s[1][c]));
-                mx2 = fmaxf(mx2, __uint_as_float(s[2][c]));
-                mx3 = fmaxf(mx3, __uint_as_float(s[3][c]));
-            }
-            const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-            m_raw = fmaxf(m_raw, mx);
-            const float m_new = mx * sl2;
-
-            // Lazy rescale: keep the old reference max unless the tile max exceeds
-            // it by more than 8 (log2 units), i.e. P entries stay <= 256.
-            const bool need = m_new > m_use + 8.0f;
-            float alpha = 1.f;
-            if (need) {
-                alpha = fast_exp2(m_use - m_new);  // 0 on the first tile
-                m_use = m_new;
-            }
-            l_sum *= alpha;
-            if (j > 0 && __any_sync(0xffffffffu, need)) {
-                uint32_t o[32];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    tmem_ld32(tO + h * 32, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                    tmem_st32(tO + h * 32, o);
-                }
-            }
-
-            const float neg_m = -m_use;
-            float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const float p0 = fast_exp2(fmaf(__uint_as_float(s[q][2 * c]), sl2, neg_m));
-                    const float p1 = fast_exp2(fmaf(__uint_as_float(s[q][2 * c + 1]), sl2, neg_m));
-                    sum0 += p0;
-                    sum1 += p1;
-                    pk[c] = pack_bf16x2(p0, p1);
-                }
-                // bf16 P column q*16.. covers S columns already consumed (32q..32q+31 >= 16q..).
-                tmem_st16(tS + q * 16, pk);
-            }
-            l_sum += sum0 + sum1;
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(bar_p);
-        }
-
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(smem_addr(&bars->o_full[t]), 0u, ctl, kSiteSoftO));
-        if (ok) {
+            // ---------------------------------------------------- epilogue of this item
+            if (!(ok = warp_wait(bar_pv, (g - 1) & 1u, ctl, kSiteSoftO))) break;
             tc_fence_after();
             uint32_t o[2][32];
             tmem_ld32(tO, o[0]);
@@ -274,9 +355,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else {
-                // Stage the bf16 tile in this tile's Q buffer (all MMAs reading it are done),
-                // in the 128-byte-swizzled image the O tensor map expects, then TMA-store it.
-                uint8_t* stage = smem + kOffQ + t * kTileBytes;
+                // bf16 tile in the 128-byte-swizzled image the O tensor map expects, then TMA store.
+                if (issuer) tma_store_wait_read0();  // the previous item's store has left the staging buffer
+                named_bar_sync(1 + t, 128);
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     const uint32_t* src = &o[c >> 2][(c & 3) * 8];
@@ -289,10 +370,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fence_proxy_async_smem();
                 named_bar_sync(1 + t, 128);
-                if ((warp & 3) == 0 && lane == 0) {
+                if (issuer) {
                     tma_store_3d(&tmO, smem_addr(stage), 0, q_row0 + t * kBM, bh);
                     tma_store_commit();
-                    tma_store_wait_read0();
                 }
             }
             if (row_ok) {
@@ -300,112 +380,178 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (p.lse) p.lse[idx] = (m_use + __log2f(l_sum)) * 0.69314718055994531f;
                 if (p.row_max) p.row_max[idx] = m_raw * p.scale;
             }
+            BF_TRACE(t, 63, 7);
         }
+        if (!kF32Out && issuer) tma_store_wait0();
     } else if (warp == 8) {
         // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            const uint32_t q_full = smem_addr(&bars->q_full);
-            mbar_arrive_expect_tx(q_full, kQTiles * kTileBytes);
-            for (int t = 0; t < kQTiles; ++t)
-                tma_load_3d(smem_addr(smem + kOffQ + t * kTileBytes), &tmQ, q_full, 0, q_row0 + t * kBM, bh);
-            int last_k = -1, last_v = -1;
-            for (int j = 0; j < nk; ++j) {
-                const int st = j % kStages;
-                const uint32_t par = ((uint32_t)(j / kStages) & 1u) ^ 1u;
-                if (!mbar_wait(smem_addr(&bars->k_empty[st]), par, ctl, kSiteProdKEmpty)) break;
-                if (!p.skip_k_loads) {
-                    mbar_arrive_expect_tx(smem_addr(&bars->k_full[st]), kTileBytes);
-                    tma_load_3d(smem_addr(smem + kOffK + st * kTileBytes), &tmK, smem_addr(&bars->k_full[st]), 0,
-                                j * kBN, bh);
-                    last_k = j;
-                }
-                if (!mbar_wait(smem_addr(&bars->v_empty[st]), par, ctl, kSiteProdVEmpty)) break;
-                mbar_arrive_expect_tx(smem_addr(&bars->v_full[st]), kTileBytes);
-                tma_load_3d(smem_addr(smem + kOffV + st * kTileBytes), &tmV, smem_addr(&bars->v_full[st]), 0,
-                            j * kBN, bh);
-                last_v = j;
+        // The whole warp runs the loop (warp-uniform control flow and
+        // addresses); one elected lane issues the copies.
+        const bool leader = elect_one();
+        const bool tracing = trace_hit && leader;
+        const uint32_t q_smem0 = smem_addr(smem + kOffQ);
+        const uint32_t k_smem0 = smem_addr(smem + kOffK), v_smem0 = smem_addr(smem + kOffV);
+        const uint32_t q_full0 = smem_addr(&bars->q_full[0]), q_empty0 = smem_addr(&bars->q_empty[0]);
+        const uint32_t k_full0 = smem_addr(&bars->k_full[0]), k_empty0 = smem_addr(&bars->k_empty[0]);
+        const uint32_t v_full0 = smem_addr(&bars->v_full[0]), v_empty0 = smem_addr(&bars->v_empty[0]);
+        int last_k = -1, last_v = -1, last_q = -1;  // for the abort drain
+        uint32_t c = 0;  // KV tiles issued by this CTA
+        int st = 0;
+        uint32_t par = 1u;  // parity of the "empty" phase to wait for (fresh barriers pass parity 1)
+        bool ok = true;
+        int it = 0;
+        for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++it) {
+            const int bh = item / p.q_blocks;
+            const int q_row0 = (item % p.q_blocks) * (kQTiles * kBM);
+            const int qb = it & 1;
+            if (!(ok = warp_wait(q_empty0 + 8 * qb, (uint32_t)((it >> 1) & 1) ^ 1u, ctl, kSiteProdQEmpty))) break;
+            if (leader) {
+                mbar_arrive_expect_tx(q_full0 + 8 * qb, kQTiles * kTileBytes);
+                for (int t = 0; t < kQTiles; ++t)
+                    tma_load_3d(q_smem0 + (qb * kQTiles + t) * kTileBytes, &tmQ, q_full0 + 8 * qb, 0,
+                                q_row0 + t * kBM, bh);
             }
-            if (*ctl.abort_flag) {
-                // Let copies still in flight land before the CTA's shared memory is released.
-                int never = 0;
-                const WaitCtl drain{&never, nullptr, ctl.limit_ns};
-                if (last_k >= 0)
-                    mbar_wait(smem_addr(&bars->k_full[last_k % kStages]), (uint32_t)(last_k / kStages) & 1u, drain, 0);
-                if (last_v >= 0)
-                    mbar_wait(smem_addr(&bars->v_full[last_v % kStages]), (uint32_t)(last_v / kStages) & 1u, drain, 0);
-                mbar_wait(smem_addr(&bars->q_full), 0u, drain, 0);
+            last_q = it;
+            __syncwarp();
+            for (int j = 0; j < nk; ++j, ++c) {
+                if (!(ok = warp_wait(k_empty0 + 8 * st, par, ctl, kSiteProdKEmpty))) break;
+                if (!p.skip_k_loads) {
+                    if (leader) {
+                        mbar_arrive_expect_tx(k_full0 + 8 * st, kTileBytes);
+                        tma_load_3d(k_smem0 + st * kTileBytes, &tmK, k_full0 + 8 * st, 0, j * kBN, bh);
+                    }
+                    BF_TRACE(3, c, 0);
+                    last_k = (int)c;
+                }
+                if (!(ok = warp_wait(v_empty0 + 8 * st, par, ctl, kSiteProdVEmpty))) break;
+                if (leader) {
+                    mbar_arrive_expect_tx(v_full0 + 8 * st, kTileBytes);
+                    tma_load_3d(v_smem0 + st * kTileBytes, &tmV, v_full0 + 8 * st, 0, j * kBN, bh);
+                }
+                BF_TRACE(3, c, 1);
+                last_v = (int)c;
+                __syncwarp();
+                if (++st == kStages) {
+                    st = 0;
+                    par ^= 1u;
+                }
             }
         }
+        if (*ctl.abort_flag) {
+            // Let copies still in flight land before the CTA's shared memory is released.
+            int never = 0;
+            const WaitCtl drain{&never, nullptr, ctl.limit_ns};
+            if (last_k >= 0) mbar_wait(k_full0 + 8 * (last_k % kStages), (uint32_t)(last_k / kStages) & 1u, drain, 0);
+            if (last_v >= 0) mbar_wait(v_full0 + 8 * (last_v % kStages), (uint32_t)(last_v / kStages) & 1u, drain, 0);
+            if (last_q >= 0) mbar_wait(q_full0 + 8 * (last_q & 1), (uint32_t)(last_q >> 1) & 1u, drain, 0);
+        }
+        __syncwarp();
     } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);  // Q (K-major) x K (K-major)
-            constexpr uint32_t kIdescO = idesc_bf16_f32(kBM, kD, 1);   // P (TMEM)   x V (MN-major)
-            const uint32_t tS0 = tmem;
-            const uint32_t tO0 = tmem + 2 * kBN;
+        // Whole warp in the loop so every descriptor and TMEM address stays
+        // warp-uniform; one elected lane issues tcgen05.mma / commit.
+        constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);  // Q (K-major) x K (K-major)
+        constexpr uint32_t kIdescO = idesc_bf16_f32(kBM, kD, 1);   // P (TMEM)   x V (MN-major)
+        const bool leader = elect_one();
+        const bool tracing = trace_hit && leader;
+        const uint32_t tS0 = tmem;
+        const uint32_t tP0 = tmem + 2 * kBN;
+        const uint32_t tO0 = tmem + 2 * kBN + 2 * kD;
+        const uint64_t q_desc0 = smem_desc_sw128(smem_addr(smem + kOffQ), 16, 1024);
+        const uint64_t k_desc0 = smem_desc_sw128(smem_addr(smem + kOffK), 16, 1024);
+        const uint64_t v_desc0 = smem_desc_sw128(smem_addr(smem + kOffV), 16, 1024);
+        constexpr uint64_t kTileDesc = kTileBytes >> 4;  // descriptor start-address step between tiles
+        const uint32_t q_full0 = smem_addr(&bars->q_full[0]), q_empty0 = smem_addr(&bars->q_empty[0]);
+        const uint32_t k_full0 = smem_addr(&bars->k_full[0]), k_empty0 = smem_addr(&bars->k_empty[0]);
+        const uint32_t v_full0 = smem_addr(&bars->v_full[0]), v_empty0 = smem_addr(&bars->v_empty[0]);
+        const uint32_t s_full0 = smem_addr(&bars->s_full[0]), s_empty0 = smem_addr(&bars->s_empty[0]);
+        const uint32_t p_full0 = smem_addr(&bars->p_full[0]), pv_done0 = smem_addr(&bars->pv_done[0]);
 
-            bool ok = mbar_wait(smem_addr(&bars->q_full), 0u, ctl, kSiteMmaQ);
-            tc_fence_after();
+        uint32_t g = 0;                  // global KV step (S issued for steps < g)
+        int kst = 0, vst = 0;            // K stage of step g, V stage of step g-1
+        uint32_t kpar = 0, vpar = 0;     // full-barrier parities for those stages
+        bool prev_first = true;          // step g-1 was the first step of its item
+        bool ok = true;
 
-            auto issue_pv = [&](int t, int vst, bool acc) {
-                const uint64_t v_desc = smem_desc_sw128(smem_addr(smem + kOffV + vst * kTileBytes), 16, 1024);
+        // O_t(g-1) += P_t(g-1) V(g-1) for both tiles.
+        auto issue_pv = [&]() -> bool {
+            const uint32_t pg = g - 1;
+            if (!warp_wait(v_full0 + 8 * vst, vpar, ctl, kSiteMmaV)) return false;
+            BF_TRACE(2, pg, 3);
+            const uint64_t v_desc = v_desc0 + (uint64_t)vst * kTileDesc;
 #pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk) {
-                    // K step of 16 KV rows: 8 TMEM columns of packed bf16 P, 16 rows x 128 B of V.
-                    umma_ts(tO0 + t * kD, tS0 + t * kBN + kk * 8, v_desc + (uint64_t)((kk * 16 * 128) >> 4), kIdescO,
-                            (acc || kk > 0) ? 1u : 0u);
-                }
-            };
-            auto issue_s = [&](int t, int kst) {
-                const uint64_t k_desc = smem_desc_sw128(smem_addr(smem + kOffK + kst * kTileBytes), 16, 1024);
-                const uint64_t q_desc = smem_desc_sw128(smem_addr(smem + kOffQ + t * kTileBytes), 16, 1024);
-#pragma unroll
-                for (int kk = 0; kk < kD / 16; ++kk) {
-                    // K step of 16 head-dim elements = 32 bytes inside the 128-byte swizzle atom.
-                    umma_ss(tS0 + t * kBN, q_desc + (uint64_t)((kk * 32) >> 4), k_desc + (uint64_t)((kk * 32) >> 4),
-                            kIdescS, kk > 0 ? 1u : 0u);
-                }
-            };
-
-            for (int j = 0; j < nk && ok; ++j) {
-                const int st = j % kStages;
-                if (!(ok = mbar_wait(smem_addr(&bars->k_full[st]), (uint32_t)(j / kStages) & 1u, ctl, kSiteMmaK)))
-                    break;
+            for (int t = 0; t < kQTiles; ++t) {
+                if (!warp_wait(p_full0 + 8 * t, pg & 1u, ctl, kSiteMmaP)) return false;
                 tc_fence_after();
-                const int pst = (j + kStages - 1) % kStages;
-                for (int t = 0; t < kQTiles && ok; ++t) {
-                    if (j > 0) {
-                        if (t == 0 && !(ok = mbar_wait(smem_addr(&bars->v_full[pst]), (uint32_t)((j - 1) / kStages) & 1u,
-                                                       ctl, kSiteMmaV)))
-                            break;
-                        if (!(ok = mbar_wait(smem_addr(&bars->p_full[t]), (uint32_t)((j - 1) & 1), ctl, kSiteMmaP)))
-                            break;
+                BF_TRACE(2, pg, 4 + t);
+                if (leader) {
+#pragma unroll
+                    for (int kk = 0; kk < kBN / 16; ++kk)  // 16 KV rows: 8 TMEM columns of P, 16 x 128 B of V
+                        umma_ts(tO0 + t * kD, tP0 + t * kD + kk * 8, v_desc + (uint64_t)(kk * 128), kIdescO,
+                                (!prev_first || kk > 0) ? 1u : 0u);
+                    umma_commit(pv_done0 + 8 * t);
+                }
+                __syncwarp();
+            }
+            if (leader) umma_commit(v_empty0 + 8 * vst);
+            __syncwarp();
+            if (++vst == kStages) {
+                vst = 0;
+                vpar ^= 1u;
+            }
+            return true;
+        };
+
+        int it = 0;
+        for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++it) {
+            const int qb = it & 1;
+            if (!(ok = warp_wait(q_full0 + 8 * qb, (uint32_t)(it >> 1) & 1u, ctl, kSiteMmaQ))) break;
+            tc_fence_after();
+            for (int j = 0; j < nk; ++j) {
+                if (!(ok = warp_wait(k_full0 + 8 * kst, kpar, ctl, kSiteMmaK))) break;
+                tc_fence_after();
+                BF_TRACE(2, g, 0);
+                const uint64_t k_desc = k_desc0 + (uint64_t)kst * kTileDesc;
+#pragma unroll
+                for (int t = 0; t < kQTiles; ++t) {
+                    if (g > 0) {
+                        if (!(ok = warp_wait(s_empty0 + 8 * t, (g - 1) & 1u, ctl, kSiteMmaSEmpty))) break;
                         tc_fence_after();
-                        issue_pv(t, pst, j - 1 > 0);
-                        if (t == kQTiles - 1) umma_commit(smem_addr(&bars->v_empty[pst]));
                     }
-                    issue_s(t, st);
-                    umma_commit(smem_addr(&bars->s_full[t]));
+                    BF_TRACE(2, g, 1 + t);
+                    if (leader) {
+                        const uint64_t q_desc = q_desc0 + (uint64_t)(qb * kQTiles + t) * kTileDesc;
+#pragma unroll
+                        for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements = 32 B within the swizzle atom
+                            umma_ss(tS0 + t * kBN, q_desc + (uint64_t)(kk * 2), k_desc + (uint64_t)(kk * 2), kIdescS,
+                                    kk > 0 ? 1u : 0u);
+                        umma_commit(s_full0 + 8 * t);
+                    }
+                    __syncwarp();
                 }
-                if (ok) umma_commit(smem_addr(&bars->k_empty[st]));
-            }
-            if (ok) {
-                const int pst = (nk - 1) % kStages;
-                ok = mbar_wait(smem_addr(&bars->v_full[pst]), (uint32_t)((nk - 1) / kStages) & 1u, ctl, kSiteMmaV);
-                for (int t = 0; t < kQTiles && ok; ++t) {
-                    if (!(ok = mbar_wait(smem_addr(&bars->p_full[t]), (uint32_t)((nk - 1) & 1), ctl, kSiteMmaP))) break;
-                    tc_fence_after();
-                    issue_pv(t, pst, nk - 1 > 0);
-                    umma_commit(smem_addr(&bars->o_full[t]));
+                if (!ok) break;
+                if (leader) {
+                    umma_commit(k_empty0 + 8 * kst);
+                    if (j == nk - 1) umma_commit(q_empty0 + 8 * qb);  // last S of this item: Q buffer free
                 }
-                if (ok) umma_commit(smem_addr(&bars->v_empty[pst]));
+                __syncwarp();
+                if (++kst == kStages) {
+                    kst = 0;
+                    kpar ^= 1u;
+                }
+                if (g > 0 && !(ok = issue_pv())) break;
+                prev_first = (j == 0);
+                ++g;
             }
-            // Drain: every MMA issued above has finished before TMEM is released.
-            umma_commit(smem_addr(&bars->drain));
-            int never = 0;
-            WaitCtl drain{&never, nullptr, ctl.limit_ns};
-            mbar_wait(smem_addr(&bars->drain), 0u, drain, 0);
         }
+        if (ok && g > 0) issue_pv();
+        // Drain: every MMA issued above has finished before TMEM is released.
+        if (leader) umma_commit(smem_addr(&bars->drain));
+        __syncwarp();
+        int never = 0;
+        const WaitCtl drain{&never, nullptr, ctl.limit_ns};
+        mbar_wait(smem_addr(&bars->drain), 0u, drain, 0);
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -469,7 +615,22 @@ int configure_once() {
 
 }  // namespace
 
+int sm_count(int* out) {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            return bf_set_error(BF_ERR_CUDA, "cannot query the SM count");
+        cached[dev] = n;
+    }
+    *out = cached[dev];
+    return BF_OK;
+}
+
 int bf_fwd_launch(const BfFwdArgs* a) {
+    int rc0;
     if (a->d != bfk::kD) return bf_set_error(BF_ERR_ARG, "BlackFlash currently only supports d=64");
     if (a->bh <= 0 || a->n_q <= 0 || a->n_kv <= 0) return bf_set_error(BF_ERR_ARG, "empty problem: B*H and N must be >= 1");
     if (!a->q || !a->k || !a->v || (!a->o && !a->o_f32)) return bf_set_error(BF_ERR_ARG, "null tensor pointer");
@@ -478,8 +639,11 @@ int bf_fwd_launch(const BfFwdArgs* a) {
         (a->o_f32 && misaligned(a->o_f32)))
         return bf_set_error(BF_ERR_ARG, "Q/K/V/O must be 16-byte aligned");
     const long long q_blocks = (a->n_q + bfk::kQTiles * bfk::kBM - 1) / (bfk::kQTiles * bfk::kBM);
-    const long long grid = q_blocks * a->bh;
-    if (grid > 0x7fffffffLL || a->bh > 0x7fffffffLL) return bf_set_error(BF_ERR_ARG, "problem too large for one launch");
+    const long long items = q_blocks * a->bh;
+    if (items > 0x7fffffffLL || a->bh > 0x7fffffffLL) return bf_set_error(BF_ERR_ARG, "problem too large for one launch");
+    int sms = 0;
+    if ((rc0 = sm_count(&sms)) != BF_OK) return rc0;
+    const long long grid = items < sms ? items : sms;  // persistent: at most one CTA per SM
 
     CUtensorMap mq, mk, mv, mo;
     int rc;
@@ -496,6 +660,7 @@ int bf_fwd_launch(const BfFwdArgs* a) {
     kp.n_q = a->n_q;
     kp.n_kv = a->n_kv;
     kp.q_blocks = (int)q_blocks;
+    kp.items = (int)items;
     kp.scale = a->scale;
     kp.scale_log2 = a->scale * 1.4426950408889634f;
     kp.lse = a->lse;
@@ -504,9 +669,22 @@ int bf_fwd_launch(const BfFwdArgs* a) {
     kp.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
     kp.dbg_s = a->dbg_s;
     kp.skip_k_loads = a->skip_k_loads;
+    kp.trace = a->trace;
+    kp.trace_cta = a->trace_cta;
 
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(a->stream);
-    if (a->o_f32) {
+    if (a->trace) {
+        if (a->o_f32) return bf_set_error(BF_ERR_ARG, "trace runs use the bf16 output");
+        static bool traced_cfg[64] = {false};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev >= 0 && dev < 64 && !traced_cfg[dev]) {
+            cudaFuncSetAttribute(bfk::fa_fwd_sm100_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 bfk::kSmemBytes);
+            traced_cfg[dev] = true;
+        }
+        bfk::fa_fwd_sm100_kernel<false, true><<<(unsigned)grid, bfk::kThreads, bfk::kSmemBytes, stream>>>(mq, mk, mv, mo, kp);
+    } else if (a->o_f32) {
         if ((rc = configure_once<true>()) != BF_OK) return rc;
         bfk::fa_fwd_sm100_kernel<true><<<(unsigned)grid, bfk::kThreads, bfk::kSmemBytes, stream>>>(mq, mk, mv, mo, kp);
     } else {

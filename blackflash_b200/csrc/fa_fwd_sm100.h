@@ -21,6 +21,8 @@ struct BfFwdArgs {
     unsigned long long timeout_ns;  // 0 = default
     float* dbg_s;
     int skip_k_loads;
+    long long* trace;
+    int trace_cta;
 };
 
 int bf_fwd_launch(const BfFwdArgs* a);

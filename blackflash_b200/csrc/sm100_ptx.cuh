@@ -75,6 +75,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     }
 }
 
+// All lanes of the (converged) warp wait; the result is warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl, unsigned int site) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, ctl, site));
+}
+
+// One lane of the (converged) warp returns true (elect.sync).
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -224,6 +240,68 @@ __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// ---- packed fp32 pairs (sm_100 f32x2 instructions): one instruction, two lanes of math
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// Three-input max (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for a pair of arguments on the FMA pipe instead of MUFU.
+// Range reduction 2^x = 2^n * 2^f, n = rint(x), f = x - n in [-1/2, 1/2]; 2^f by a
+// degree-3 polynomial with minimax relative error 7.5e-5 (coefficients from
+// csrc/fit_exp2.py, Lawson's algorithm); 2^n applied by adding n to the exponent
+// field. Arguments are clamped to >= -126: with p(f) in [0.70, 1.42] the biased
+// exponent then stays >= 0 (a denormal at worst) and cannot wrap into the sign
+// bit; ~2^-126 stands in for 0 (it rounds to 0 in the bf16 P).
+constexpr float kExp2C0 = 0.9999281167984009f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.24261054396629333f;
+constexpr float kExp2C3 = 0.05517132207751274f;
+
+__device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x2) {
+    float x0, x1;
+    f2_unpack(x2, x0, x1);
+    x2 = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+    const uint64_t magic = f2_pack(12582912.f, 12582912.f);  // 1.5 * 2^23: x + magic rounds x to an integer
+    const uint64_t t = f2_add(x2, magic);
+    const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+    const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x2);
+    uint64_t p = f2_fma(f, f2_pack(kExp2C3, kExp2C3), f2_pack(kExp2C2, kExp2C2));
+    p = f2_fma(p, f, f2_pack(kExp2C1, kExp2C1));
+    p = f2_fma(p, f, f2_pack(kExp2C0, kExp2C0));
+    // n sits in the low mantissa bits of t; shifting left by 23 moves it into the exponent field.
+    uint32_t t0, t1, p0, p1;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t));
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(p0), "=r"(p1) : "l"(p));
+    uint32_t r0, r1;
+    asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(r0) : "r"(t0), "r"(p0));
+    asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(r1) : "r"(t1), "r"(p1));
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(r0), "r"(r1));
+    return r;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

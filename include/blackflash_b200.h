@@ -85,6 +85,16 @@ int blackflash_fwd_timeout_probe(const void* Q, const void* K, const void* V, vo
 int blackflash_fwd_debug_s(const void* Q, const void* K, const void* V, void* O, float* dbg_s, int B, int H, int N,
                            int d, float scale, void* stream);
 
+/*
+ * Diagnostic hook: the same launch as blackflash_fwd, built with pipeline event
+ * stamps. For CTA `trace_cta` it writes clock64() offsets into trace[4 * 512]
+ * (int64, caller-zeroed): trace[role * 512 + step * 8 + event] for the CTA's
+ * first 64 KV steps, roles 0/1 = softmax warpgroups, 2 = MMA issuer, 3 = TMA
+ * producer. No counterpart in the reference.
+ */
+int blackflash_fwd_trace(const void* Q, const void* K, const void* V, void* O, long long* trace, int trace_cta, int B,
+                         int H, int N, int d, float scale, void* stream);
+
 /* Message for the last error returned on this thread ("" if none). */
 const char* blackflash_last_error(void);
 

@@ -14,7 +14,7 @@
 //     shuffles. They also rescale O in TMEM (lazily) and run the epilogue;
 //   * warp 8: TMA producer: Q (double-buffered across items) and K / V per
 //     128-row KV tile into a kStages-deep mbarrier ring, 128-byte swizzle;
-//   * warp 9: allocates TMEM and issues every tcgen05.mma:
+//   * warps 9 / 10: issue the tcgen05.mma streams (S / PV), warp 9 owns TMEM:
 //       S_t = Q_t K_j^T   (M=128, N=128, K=64; A,B from smem)      -> TMEM
 //       O_t += P_t V_j    (M=128, N=64,  K=128; A=P from TMEM, B=V) -> TMEM
 //     P_t is written by the softmax threads as bf16 into its own TMEM
@@ -22,8 +22,8 @@
 // TMEM columns (all 512): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 //                         O0 [384,448) O1 [448,512).
 //
-// Pipelining. The MMA issuer walks one flat stream of KV steps across work
-// items: S(g) for both tiles, then PV(g-1) for both tiles. A softmax
+// Pipelining. Each MMA issuer walks one flat stream of KV steps across work
+// items (S(g) for both tiles; PV(g) for both tiles). A softmax
 // warpgroup releases S_t (s_empty) as soon as S_t(g) is in registers, so the
 // tensor core computes S_t(g+1) - possibly the next item's - while the
 // exponentials of step g run; it waits for PV_t(g-1) (pv_done) only before it
@@ -57,6 +57,9 @@ constexpr int kStages = 3;      // K/V ring depth
 constexpr int kThreads = 384;
 constexpr int kTileBytes = kBM * kD * 2;  // 16 KiB (Q, K, V or O tile, bf16)
 constexpr int kTmemCols = 512;
+constexpr int kProducerWarp = 8;  // TMA producer
+constexpr int kSWarp = 9;         // issues S = Q K^T; owns the TMEM allocation
+constexpr int kPVWarp = 10;       // issues O += P V
 #ifndef BF_EMU_PAIRS
 #define BF_EMU_PAIRS 2
 #endif
@@ -81,6 +84,7 @@ struct Bars {
     uint64_t p_full[kQTiles];
     uint64_t pv_done[kQTiles];
     uint64_t drain;
+    uint64_t drain_pv;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -93,10 +97,8 @@ enum : unsigned {
     kSiteProdKEmpty = 0x101,
     kSiteProdVEmpty = 0x102,
     kSiteMmaQ = 0x201,
-    kSiteMmaK = 0x202,
-    kSiteMmaV = 0x203,
-    kSiteMmaP = 0x204,
-    kSiteMmaSEmpty = 0x205,
+    kSiteMmaK = 0x210,  // +0 K full, +1 S_0 empty, +2 S_1 empty
+    kSiteMmaV = 0x220,  // +0 V full, +1 P_0 full, +2 P_1 full
     kSiteSoftS = 0x301,
     kSiteSoftO = 0x302,
     kSiteSoftPV = 0x303,
@@ -167,16 +169,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_addr(&bars->pv_done[t]), 1);
         }
         mbar_init(smem_addr(&bars->drain), 1);
+        mbar_init(smem_addr(&bars->drain_pv), 1);
         bars->abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 8 && lane == 0) {
+    if (warp == kProducerWarp && lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
         if (!kF32Out) tma_prefetch_desc(&tmO);
     }
-    if (warp == 9) {
+    if (warp == kSWarp) {
         tmem_alloc(smem_addr(&bars->tmem_base), kTmemCols);
         tmem_relinquish();
     }
@@ -383,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             BF_TRACE(t, 63, 7);
         }
         if (!kF32Out && issuer) tma_store_wait0();
-    } else if (warp == 8) {
+    } else if (warp == kProducerWarp) {
         // ------------------------------------------------------------ TMA producer
         // The whole warp runs the loop (warp-uniform control flow and
         // addresses); one elected lane issues the copies.
@@ -446,117 +449,105 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (last_q >= 0) mbar_wait(q_full0 + 8 * (last_q & 1), (uint32_t)(last_q >> 1) & 1u, drain, 0);
         }
         __syncwarp();
-    } else if (warp == 9) {
-        // ------------------------------------------------------------ MMA issuer
-        // Whole warp in the loop so every descriptor and TMEM address stays
-        // warp-uniform; one elected lane issues tcgen05.mma / commit.
+    } else if (warp == kSWarp || warp == kPVWarp) {
+        // ------------------------------------------------------------ MMA issuers
+        // Two warps on different schedulers issue the two independent MMA
+        // streams: warp kSWarp S_t = Q_t K^T, warp kPVWarp O_t += P_t V. Each
+        // whole warp runs its loop (warp-uniform values), waits for all the
+        // barriers of a step in one parallel round, and one elected lane issues.
+        // Keeping these loops short matters: they share their schedulers with
+        // busy softmax warps, and the tensor core's issue queue is shallow.
         constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);  // Q (K-major) x K (K-major)
         constexpr uint32_t kIdescO = idesc_bf16_f32(kBM, kD, 1);   // P (TMEM)   x V (MN-major)
         const bool leader = elect_one();
         const bool tracing = trace_hit && leader;
-        const uint32_t tS0 = tmem;
-        const uint32_t tP0 = tmem + 2 * kBN;
-        const uint32_t tO0 = tmem + 2 * kBN + 2 * kD;
-        const uint64_t q_desc0 = smem_desc_sw128(smem_addr(smem + kOffQ), 16, 1024);
-        const uint64_t k_desc0 = smem_desc_sw128(smem_addr(smem + kOffK), 16, 1024);
-        const uint64_t v_desc0 = smem_desc_sw128(smem_addr(smem + kOffV), 16, 1024);
-        constexpr uint64_t kTileDesc = kTileBytes >> 4;  // descriptor start-address step between tiles
+        const uint64_t desc_base = smem_desc_sw128(smem_addr(smem), 16, 1024);
+        const uint32_t desc_hi = (uint32_t)(desc_base >> 32);
+        const uint32_t desc_lo0 = (uint32_t)desc_base;  // low word of a descriptor at smem offset 0
+        constexpr uint32_t kTileLo = kTileBytes >> 4;   // low-word step between 16 KiB tiles
+        const uint32_t q_lo0 = desc_lo0 + (kOffQ >> 4), k_lo0 = desc_lo0 + (kOffK >> 4), v_lo0 = desc_lo0 + (kOffV >> 4);
         const uint32_t q_full0 = smem_addr(&bars->q_full[0]), q_empty0 = smem_addr(&bars->q_empty[0]);
         const uint32_t k_full0 = smem_addr(&bars->k_full[0]), k_empty0 = smem_addr(&bars->k_empty[0]);
         const uint32_t v_full0 = smem_addr(&bars->v_full[0]), v_empty0 = smem_addr(&bars->v_empty[0]);
         const uint32_t s_full0 = smem_addr(&bars->s_full[0]), s_empty0 = smem_addr(&bars->s_empty[0]);
         const uint32_t p_full0 = smem_addr(&bars->p_full[0]), pv_done0 = smem_addr(&bars->pv_done[0]);
+        const bool is_s = warp == kSWarp;
 
-        uint32_t g = 0;                  // global KV step (S issued for steps < g)
-        int kst = 0, vst = 0;            // K stage of step g, V stage of step g-1
-        uint32_t kpar = 0, vpar = 0;     // full-barrier parities for those stages
-        bool prev_first = true;          // step g-1 was the first step of its item
+        uint32_t g = 0;          // global KV step
+        int st = 0;              // K (S warp) or V (PV warp) stage of step g
+        uint32_t par = 0;        // its full-barrier parity
         bool ok = true;
-
-        // O_t(g-1) += P_t(g-1) V(g-1) for both tiles.
-        auto issue_pv = [&]() -> bool {
-            const uint32_t pg = g - 1;
-            if (!warp_wait(v_full0 + 8 * vst, vpar, ctl, kSiteMmaV)) return false;
-            BF_TRACE(2, pg, 3);
-            const uint64_t v_desc = v_desc0 + (uint64_t)vst * kTileDesc;
-#pragma unroll
-            for (int t = 0; t < kQTiles; ++t) {
-                if (!warp_wait(p_full0 + 8 * t, pg & 1u, ctl, kSiteMmaP)) return false;
-                tc_fence_after();
-                BF_TRACE(2, pg, 4 + t);
-                if (leader) {
-#pragma unroll
-                    for (int kk = 0; kk < kBN / 16; ++kk)  // 16 KV rows: 8 TMEM columns of P, 16 x 128 B of V
-                        umma_ts(tO0 + t * kD, tP0 + t * kD + kk * 8, v_desc + (uint64_t)(kk * 128), kIdescO,
-                                (!prev_first || kk > 0) ? 1u : 0u);
-                    umma_commit(pv_done0 + 8 * t);
-                }
-                __syncwarp();
-            }
-            if (leader) umma_commit(v_empty0 + 8 * vst);
-            __syncwarp();
-            if (++vst == kStages) {
-                vst = 0;
-                vpar ^= 1u;
-            }
-            return true;
-        };
-
         int it = 0;
         for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++it) {
             const int qb = it & 1;
-            if (!(ok = warp_wait(q_full0 + 8 * qb, (uint32_t)(it >> 1) & 1u, ctl, kSiteMmaQ))) break;
-            tc_fence_after();
-            for (int j = 0; j < nk; ++j) {
-                if (!(ok = warp_wait(k_full0 + 8 * kst, kpar, ctl, kSiteMmaK))) break;
+            if (is_s) {
+                if (!(ok = warp_wait(q_full0 + 8 * qb, (uint32_t)(it >> 1) & 1u, ctl, kSiteMmaQ))) break;
                 tc_fence_after();
-                BF_TRACE(2, g, 0);
-                const uint64_t k_desc = k_desc0 + (uint64_t)kst * kTileDesc;
-#pragma unroll
-                for (int t = 0; t < kQTiles; ++t) {
-                    if (g > 0) {
-                        if (!(ok = warp_wait(s_empty0 + 8 * t, (g - 1) & 1u, ctl, kSiteMmaSEmpty))) break;
-                        tc_fence_after();
-                    }
-                    BF_TRACE(2, g, 1 + t);
+            }
+            for (int j = 0; j < nk; ++j, ++g) {
+                if (is_s) {
+                    // K(g) loaded, S_0 and S_1 read out by the softmax.
+                    if (!(ok = warp_wait_n(g > 0 ? 3 : 1, k_full0 + 8 * st, par, s_empty0, (g - 1) & 1u, s_empty0 + 8,
+                                           (g - 1) & 1u, ctl, kSiteMmaK)))
+                        break;
+                    tc_fence_after();
+                    BF_TRACE(2, g, 0);
                     if (leader) {
-                        const uint64_t q_desc = q_desc0 + (uint64_t)(qb * kQTiles + t) * kTileDesc;
+                        const uint32_t k_lo = k_lo0 + (uint32_t)st * kTileLo;
 #pragma unroll
-                        for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements = 32 B within the swizzle atom
-                            umma_ss(tS0 + t * kBN, q_desc + (uint64_t)(kk * 2), k_desc + (uint64_t)(kk * 2), kIdescS,
-                                    kk > 0 ? 1u : 0u);
-                        umma_commit(s_full0 + 8 * t);
+                        for (int t = 0; t < kQTiles; ++t) {
+                            const uint32_t q_lo = q_lo0 + (uint32_t)(qb * kQTiles + t) * kTileLo;
+#pragma unroll
+                            for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements = 32 B inside the swizzle atom
+                                umma_ss_lo(tmem + t * kBN, q_lo + kk * 2, k_lo + kk * 2, desc_hi, kIdescS, kk > 0);
+                            umma_commit(s_full0 + 8 * t);
+                        }
+                        umma_commit(k_empty0 + 8 * st);
+                        if (j == nk - 1) umma_commit(q_empty0 + 8 * qb);  // last S of this item: Q buffer free
                     }
                     __syncwarp();
+                    BF_TRACE(2, g, 1);
+                } else {
+                    // V(g) loaded, P_0(g) and P_1(g) written by the softmax.
+                    if (!(ok = warp_wait_n(3, v_full0 + 8 * st, par, p_full0, g & 1u, p_full0 + 8, g & 1u, ctl,
+                                           kSiteMmaV)))
+                        break;
+                    tc_fence_after();
+                    BF_TRACE(2, g, 2);
+                    if (leader) {
+                        const uint32_t v_lo = v_lo0 + (uint32_t)st * kTileLo;
+#pragma unroll
+                        for (int t = 0; t < kQTiles; ++t) {
+#pragma unroll
+                            for (int kk = 0; kk < kBN / 16; ++kk)  // 16 KV rows: 8 TMEM columns of P, 16 x 128 B of V
+                                umma_ts_lo(tmem + 2 * kBN + 2 * kD + t * kD, tmem + 2 * kBN + t * kD + kk * 8,
+                                           v_lo + kk * 128, desc_hi, kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+                            umma_commit(pv_done0 + 8 * t);
+                        }
+                        umma_commit(v_empty0 + 8 * st);
+                    }
+                    __syncwarp();
+                    BF_TRACE(2, g, 3);
                 }
-                if (!ok) break;
-                if (leader) {
-                    umma_commit(k_empty0 + 8 * kst);
-                    if (j == nk - 1) umma_commit(q_empty0 + 8 * qb);  // last S of this item: Q buffer free
+                if (++st == kStages) {
+                    st = 0;
+                    par ^= 1u;
                 }
-                __syncwarp();
-                if (++kst == kStages) {
-                    kst = 0;
-                    kpar ^= 1u;
-                }
-                if (g > 0 && !(ok = issue_pv())) break;
-                prev_first = (j == 0);
-                ++g;
             }
         }
-        if (ok && g > 0) issue_pv();
-        // Drain: every MMA issued above has finished before TMEM is released.
-        if (leader) umma_commit(smem_addr(&bars->drain));
+        // Drain: every MMA this warp issued has finished before TMEM is released.
+        const uint32_t drain_bar = smem_addr(is_s ? &bars->drain : &bars->drain_pv);
+        if (leader) umma_commit(drain_bar);
         __syncwarp();
         int never = 0;
         const WaitCtl drain{&never, nullptr, ctl.limit_ns};
-        mbar_wait(smem_addr(&bars->drain), 0u, drain, 0);
+        mbar_wait(drain_bar, 0u, drain, 0);
         __syncwarp();
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == kSWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }

@@ -51,6 +51,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware (it issues
+// nothing) until the phase completes or about `hint_ns` pass.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Shared state for bounded waits. A wait that exceeds `limit_ns` records
 // `site` in the global status word (first writer wins), raises the CTA-wide
 // abort flag, and returns false; every other wait in the CTA then gives up at
@@ -65,7 +79,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        // A sleeping wait issues nothing, leaving the scheduler to the warps that
+        // share it (the MMA issuers in particular must not be starved).
+        if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
         if (*ctl.abort_flag) return false;
         if (global_timer_ns() - t0 > ctl.limit_ns) {
             *ctl.abort_flag = 1;
@@ -89,6 +105,20 @@ __device__ __forceinline__ bool elect_one() {
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(pred));
     return pred != 0;
+}
+
+// Up to three barriers waited in parallel: lane i polls (bar[i], parity[i]) for
+// i < n, the other lanes pass at once; one vote makes the result warp-uniform.
+__device__ __forceinline__ bool warp_wait_n(int n, uint32_t b0, uint32_t p0, uint32_t b1, uint32_t p1, uint32_t b2,
+                                            uint32_t p2, const WaitCtl& ctl, unsigned int site) {
+    const int lane = threadIdx.x & 31;
+    bool ok = true;
+    if (lane < n) {
+        const uint32_t bar = lane == 0 ? b0 : (lane == 1 ? b1 : b2);
+        const uint32_t par = lane == 0 ? p0 : (lane == 1 ? p1 : p2);
+        ok = mbar_wait(bar, par, ctl, site + (unsigned)lane);
+    }
+    return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------- TMA
@@ -156,6 +186,31 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Same as umma_ss / umma_ts with the two shared-memory descriptors given as a
+// varying low word and a shared high word (all descriptors here share the high
+// word: SBO, version and swizzle), so the issue loop carries 32-bit values only.
+__device__ __forceinline__ void umma_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\t"
+        "mov.b64 a, {%1, %3};\n\t"
+        "mov.b64 b, {%2, %3};\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %4, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 b;\n\t"
+        "mov.b64 b, {%2, %3};\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], b, %4, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 

@@ -1,0 +1,92 @@
+"""Sequence-parallel (ring) path on GPUs.
+
+Single GPU: the ring's compute - partial attention per KV block, log-sum-exp
+merge, bf16 cast - run over G blocks in one process must equal the full forward
+and the oracle. Two or more GPUs: the real schedule over NCCL (one process per
+GPU, P2P send/recv), checked against the oracle."""
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def test_partial_merge_equals_full_attention():
+    from blackflash_b200 import attention_partial, forward_lse, lse_merge_, to_bf16
+    from blackflash_b200.inputs import make_qkv
+    S, N, G = 6, 1536, 4
+    q, k, v = make_qkv(1, S, N, dist="peaked", seed=31, device="cuda")
+    q3, k3, v3 = (t.reshape(S, N, 64) for t in (q, k, v))
+    blk = N // G
+    o_acc = lse_acc = None
+    for b in range(G):
+        o_p, l_p = attention_partial(q3, k3[:, b * blk:(b + 1) * blk].contiguous(),
+                                     v3[:, b * blk:(b + 1) * blk].contiguous(), 0.125)
+        if o_acc is None:
+            o_acc, lse_acc = o_p, l_p
+        else:
+            lse_merge_(o_acc, lse_acc, o_p, l_p)
+    o_ring = to_bf16(o_acc)
+    O, lse, _ = forward_lse(q, k, v, 0.125)
+    torch.cuda.synchronize()
+    o_ref, lse_ref, _ = oracle.attn_exact(q3.cpu(), k3.cpu(), v3.cpu(), 0.125)
+    d = np.abs(o_ring.float().cpu().numpy() - o_ref)
+    assert d.max() <= 1e-2 and d.mean() <= 1e-3
+    np.testing.assert_allclose(lse_acc.cpu().numpy(), lse_ref, atol=2e-3)
+    assert (o_ring.float() - O.reshape(S, N, 64).float()).abs().max().item() <= 1e-2
+
+
+def test_partial_ragged_blocks():
+    """Partial attention with Nq != Nkv and ragged sizes (the masked KV tail)."""
+    from blackflash_b200 import attention_partial
+    from blackflash_b200.inputs import make_qkv
+    q, _, _ = make_qkv(1, 3, 300, seed=1, device="cuda")
+    _, k, v = make_qkv(1, 3, 457, seed=2, device="cuda")
+    q3, k3, v3 = q.reshape(3, 300, 64), k.reshape(3, 457, 64), v.reshape(3, 457, 64)
+    o, lse = attention_partial(q3, k3, v3, 0.125)
+    torch.cuda.synchronize()
+    o_ref, lse_ref, _ = oracle.attn_exact(q3.cpu(), k3.cpu(), v3.cpu(), 0.125)
+    assert np.abs(o.cpu().numpy() - o_ref).max() <= 1e-2
+    np.testing.assert_allclose(lse.cpu().numpy(), lse_ref, atol=2e-3)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ring_worker(rank, world, port, qkv, out):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from blackflash_b200.ring import ring_attention
+    q, k, v = (t.cuda() for t in qkv)
+    n = q.shape[1] // world
+    sl = slice(rank * n, (rank + 1) * n)
+    o = ring_attention(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125)
+    torch.save(o.cpu(), f"{out}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+def test_ring_over_nccl(tmp_path):
+    from blackflash_b200.inputs import make_qkv
+    world = min(torch.cuda.device_count(), 4)
+    S, N = 4, 512 * world
+    q, k, v = (t.reshape(S, N, 64) for t in make_qkv(1, S, N, seed=77))
+    out = str(tmp_path / "ring")
+    mp.spawn(_ring_worker, args=(world, _free_port(), (q, k, v), out), nprocs=world, join=True)
+    o = torch.cat([torch.load(f"{out}.{r}") for r in range(world)], dim=1).float().numpy()
+    o_ref, _, _ = oracle.attn_exact(q, k, v, 0.125)
+    d = np.abs(o - o_ref)
+    assert d.max() <= 1e-2 and d.mean() <= 1e-3

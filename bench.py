@@ -42,6 +42,8 @@ CONFIGS = {
     "2": (4, 8, 1024, 64, "normal"),
     "3": (64, 64, 1024, 64, "normal"),
     "4": (8, 16, 8192, 64, "peaked"),
+    # long sequence: sequence-sharded over the ranks, KV rotated ring-style over NCCL, LSE merge
+    "5": (1, 32, 65536, 64, "normal"),
     # profiling case: same per-slice shape as config 3, 1/4 of the slices (1.6 GB device memory)
     "prof": (16, 64, 1024, 64, "normal"),
 }
@@ -135,13 +137,17 @@ def dist_env():
 
 def cpu_reference_sample(B, H, N, d, dist, budget_s: float, seed: int = 0):
     """Reference CPU path (torch fp32 math, tests/test_blackflash.py:16-19) on a bounded
-    sample of the workload's slices; returns (TFLOPS, slices, seconds, threads)."""
+    sample of the workload: whole (b,h) slices, and for long sequences a block of at
+    most 2048 query rows per slice against all N keys. Returns
+    (TFLOPS, sample description, seconds, threads)."""
     from blackflash_b200.inputs import make_qkv
     from oracle import oracle
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    chunk = 4
+    chunk = 4 if N <= 8192 else 1
+    rows = min(N, 2048)
     q, k, v = make_qkv(1, chunk, N, d, dist=dist, seed=seed)
+    q = q[:, :, :rows].contiguous()
     oracle.torch_math(q, k, v, 1.0 / math.sqrt(d))  # warm-up
     done, t0 = 0, time.perf_counter()
     while True:
@@ -150,7 +156,8 @@ def cpu_reference_sample(B, H, N, d, dist, budget_s: float, seed: int = 0):
         el = time.perf_counter() - t0
         if el >= budget_s or done >= B * H:
             break
-    return flops(1, done, N, d) / el / 1e12, done, el, torch.get_num_threads()
+    sample = f"{done} of {B*H} (b,h) slices" + (f", {rows} of {N} query rows each" if rows < N else "")
+    return 4.0 * done * rows * N * d / el / 1e12, sample, el, torch.get_num_threads()
 
 
 def run_reference(args, cfg_name):
@@ -161,14 +168,13 @@ def run_reference(args, cfg_name):
     per_step = []
     for _ in range(args.warmup):
         cpu_reference_sample(B, H, N, d, dist, budget_s=0.5)
-    slices = 0
+    desc = ""
     threads = 1
     for _ in range(args.steps):
-        tf, n_sl, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.ref_step_seconds)
+        tf, desc, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.ref_step_seconds)
         per_step.append(tf)
-        slices = n_sl
     value = statistics.mean(per_step)
-    sample = f"{slices} of {B*H} (b,h) slices per step, N={N}, torch fp32 CPU math; TFLOPS scaled per slice"
+    sample = f"{desc} per step, N={N}, torch fp32 CPU math; TFLOPS = 4*rows*N*d per sampled slice / time"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup,
@@ -284,9 +290,9 @@ def run_ours(args, cfg_name):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tf, n_sl, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.cpu_seconds)
+        tf, desc, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.cpu_seconds)
         cpu = {"value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",
-               "sample": f"{n_sl} of {total} (b,h) slices of the same workload, torch fp32 CPU math "
+               "sample": f"{desc} of the same workload, torch fp32 CPU math "
                          f"(reference tests/test_blackflash.py:16-19), {el:.1f} s"}
 
     if rank == 0:
@@ -316,6 +322,118 @@ def run_ours(args, cfg_name):
         dist_mod.destroy_process_group()
 
 
+def run_ring(args, cfg_name):
+    """Config 5: the sequence is split over the ranks; each step is one full ring pass
+    (world partial kernels, world-1 LSE merges, one bf16 cast per rank) with the next
+    KV block's NCCL send/recv overlapping the current block's kernel."""
+    import torch.distributed as dist_mod
+
+    from blackflash_b200.inputs import make_qkv
+    from blackflash_b200.ring import ring_attention
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist_mod.init_process_group("nccl", device_id=dev)
+    B, H, N, d, dist = CONFIGS[cfg_name]
+    if N % world:
+        raise SystemExit("N must divide evenly over the ranks")
+    n_loc = N // world
+    q, k, v = (t.reshape(B * H, n_loc, d) for t in make_qkv(B, H, n_loc, d, dist=dist, seed=2000 + rank, device=dev))
+    scale = 1.0 / math.sqrt(d)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return ring_attention(q, k, v, scale)
+
+    def barrier():
+        if world > 1:
+            dist_mod.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist_mod.all_reduce(t, op=dist_mod.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    h1 = time.time()
+    barrier()
+    sampler.stop()
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    f_total = flops(B, H, N, d)
+    value = f_total / (ms_step * 1e-3) / 1e12
+
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    oh = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+
+    def e2e_step():
+        o = ring_attention(qh.to(dev, non_blocking=True), kh.to(dev, non_blocking=True),
+                           vh.to(dev, non_blocking=True), scale)
+        oh.copy_(o, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, desc, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.cpu_seconds)
+        cpu = {"value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",
+               "sample": f"{desc} of the same workload, torch fp32 CPU math, {el:.1f} s"}
+    if rank == 0:
+        peaks = load_peaks()
+        per_gpu = value / world
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal, sequence-parallel ring",
+                       "global_batch": B, "seq_len": N, "parallelism": f"ring{world} (NCCL send/recv, LSE merge)",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": per_gpu / peaks["bf16_tflops"], "traffic": None,
+                         "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
+                         "kernel": "fa_fwd_sm100_kernel (fp32 partial mode)"},
+            "cpu_baseline": cpu,
+            "clocks": sampler.summary(h0, h1),
+            "e2e": {"value": f_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+                    "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": q.numel() * 2,
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": args.steps * (2 * world),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist_mod.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -332,6 +450,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args, args.config)
+    elif args.config == "5":
+        run_ring(args, args.config)
     else:
         run_ours(args, args.config)
 

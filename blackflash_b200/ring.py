@@ -51,15 +51,18 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
     q, k, v: [S, n_local, 64] bf16 (S = B*H slices), this rank's sequence block.
     Returns bf16 O [S, n_local, 64] (and the fp32 lse [S, n_local] if return_lse).
     """
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
+    if dist.is_available() and dist.is_initialized():
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+    else:
+        world, rank = 1, 0  # one process: the ring degenerates to a single partial step
     if k.shape != v.shape or q.shape[0] != k.shape[0]:
         raise RuntimeError("ring_attention: q [S,n,64] and k, v [S,m,64] with equal S required")
     nxt = dist.get_global_rank(group, (rank + 1) % world) if group is not None else (rank + 1) % world
     prv = dist.get_global_rank(group, (rank - 1) % world) if group is not None else (rank - 1) % world
 
     cur_k, cur_v = k, v
-    spare = [(torch.empty_like(k), torch.empty_like(v)), (torch.empty_like(k), torch.empty_like(v))]
+    n_spare = min(2, world - 1)
+    spare = [(torch.empty_like(k), torch.empty_like(v)) for _ in range(n_spare)]
     o_acc = lse_acc = None
     for step in range(world):
         reqs = []

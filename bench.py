@@ -49,9 +49,11 @@ CONFIGS = {
 }
 METRIC = "attention fwd TFLOPS (4BHN^2d/t)"
 
-# DRAM traffic per launch of the main kernel, from ncu (profiles/fa_fwd_sm100_b64h64n1024.txt):
-# bytes read + written for one full launch of config 3 at N=1. None until measured.
-TRAFFIC_BYTES = {"3": None}
+# DRAM bytes (read + write) per launch of the main kernel for config 3 at N=1. Measured by
+# ncu on a quarter-size case (profiles/fa_fwd_sm100_b16h64n1024.md: 402.7 MB read +
+# 114.2 MB written for 1024 slices) and scaled by 4; traffic is linear in the slice count
+# because every slice is independent.
+TRAFFIC_BYTES = {"3": 4 * (402.701312e6 + 114.199296e6)}
 
 
 def flops(B, H, N, d):

@@ -60,6 +60,16 @@ constexpr int kTmemCols = 512;
 constexpr int kProducerWarp = 8;  // TMA producer
 constexpr int kSWarp = 9;         // issues S = Q K^T; owns the TMEM allocation
 constexpr int kPVWarp = 10;       // issues O += P V
+#ifndef BF_PINGPONG
+#define BF_PINGPONG 0
+#endif
+// Ping-pong (off by default: measured 2 % slower than free-running warpgroups
+// on B200, kept as a build option): the two softmax warpgroups take turns for their exponential phase
+// (warpgroup 0 of step g, then warpgroup 1 of step g, then warpgroup 0 of step
+// g+1, ...). Each one's exponentials then run with MUFU to itself while the
+// other loads S, reduces the max and stores P, instead of both fighting over
+// MUFU at the same time and leaving it idle together.
+constexpr bool kPingPong = BF_PINGPONG != 0;
 #ifndef BF_EMU_PAIRS
 #define BF_EMU_PAIRS 2
 #endif
@@ -83,6 +93,7 @@ struct Bars {
     uint64_t s_empty[kQTiles];
     uint64_t p_full[kQTiles];
     uint64_t pv_done[kQTiles];
+    uint64_t exp_turn[kQTiles];  // ping-pong: warpgroup t may start its exponentials
     uint64_t drain;
     uint64_t drain_pv;
     uint32_t tmem_base;
@@ -102,6 +113,7 @@ enum : unsigned {
     kSiteSoftS = 0x301,
     kSiteSoftO = 0x302,
     kSiteSoftPV = 0x303,
+    kSiteSoftTurn = 0x304,
 };
 
 struct KParams {
@@ -167,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_addr(&bars->s_empty[t]), kBM);
             mbar_init(smem_addr(&bars->p_full[t]), kBM);
             mbar_init(smem_addr(&bars->pv_done[t]), 1);
+            mbar_init(smem_addr(&bars->exp_turn[t]), kBM);
         }
         mbar_init(smem_addr(&bars->drain), 1);
         mbar_init(smem_addr(&bars->drain_pv), 1);
@@ -275,6 +288,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 l_sum *= alpha;
 
+                if (kPingPong && (t == 1 || g > 0)) {
+                    const uint32_t turn_par = t == 0 ? ((g - 1) & 1u) : (g & 1u);
+                    if (!(ok = warp_wait(smem_addr(&bars->exp_turn[t]), turn_par, ctl, kSiteSoftTurn))) break;
+                }
                 const uint64_t negm_2 = f2_pack(-m_use, -m_use);
                 uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = f2_pack(0.f, 0.f);
                 uint32_t pk[4][16];
@@ -307,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     f2_unpack(sum_b, b0, b1);
                     l_sum += (a0 + a1) + (b0 + b1);
                 }
+                if (kPingPong) mbar_arrive(smem_addr(&bars->exp_turn[1 - t]));  // hand MUFU to the other warpgroup
                 BF_TRACE(t, g, 4);
 
                 // P_t of the previous step must have been consumed (and O_t be final)
@@ -486,46 +504,54 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             for (int j = 0; j < nk; ++j, ++g) {
                 if (is_s) {
-                    // K(g) loaded, S_0 and S_1 read out by the softmax.
-                    if (!(ok = warp_wait_n(g > 0 ? 3 : 1, k_full0 + 8 * st, par, s_empty0, (g - 1) & 1u, s_empty0 + 8,
-                                           (g - 1) & 1u, ctl, kSiteMmaK)))
-                        break;
+                    // K(g) loaded; then each S_t is issued as soon as its softmax has read S_t(g-1),
+                    // so the two tiles may run half a step apart (ping-pong).
+                    if (!(ok = warp_wait(k_full0 + 8 * st, par, ctl, kSiteMmaK))) break;
                     tc_fence_after();
                     BF_TRACE(2, g, 0);
-                    if (leader) {
-                        const uint32_t k_lo = k_lo0 + (uint32_t)st * kTileLo;
+                    const uint32_t k_lo = k_lo0 + (uint32_t)st * kTileLo;
 #pragma unroll
-                        for (int t = 0; t < kQTiles; ++t) {
+                    for (int t = 0; t < kQTiles; ++t) {
+                        if (g > 0) {
+                            if (!(ok = warp_wait(s_empty0 + 8 * t, (g - 1) & 1u, ctl, kSiteMmaK + 1 + t))) break;
+                            tc_fence_after();
+                        }
+                        if (leader) {
                             const uint32_t q_lo = q_lo0 + (uint32_t)(qb * kQTiles + t) * kTileLo;
 #pragma unroll
                             for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements = 32 B inside the swizzle atom
                                 umma_ss_lo(tmem + t * kBN, q_lo + kk * 2, k_lo + kk * 2, desc_hi, kIdescS, kk > 0);
                             umma_commit(s_full0 + 8 * t);
                         }
+                        __syncwarp();
+                    }
+                    if (!ok) break;
+                    if (leader) {
                         umma_commit(k_empty0 + 8 * st);
                         if (j == nk - 1) umma_commit(q_empty0 + 8 * qb);  // last S of this item: Q buffer free
                     }
                     __syncwarp();
                     BF_TRACE(2, g, 1);
                 } else {
-                    // V(g) loaded, P_0(g) and P_1(g) written by the softmax.
-                    if (!(ok = warp_wait_n(3, v_full0 + 8 * st, par, p_full0, g & 1u, p_full0 + 8, g & 1u, ctl,
-                                           kSiteMmaV)))
-                        break;
-                    tc_fence_after();
+                    // V(g) loaded; then each PV_t as soon as P_t(g) is written.
+                    if (!(ok = warp_wait(v_full0 + 8 * st, par, ctl, kSiteMmaV))) break;
                     BF_TRACE(2, g, 2);
-                    if (leader) {
-                        const uint32_t v_lo = v_lo0 + (uint32_t)st * kTileLo;
+                    const uint32_t v_lo = v_lo0 + (uint32_t)st * kTileLo;
 #pragma unroll
-                        for (int t = 0; t < kQTiles; ++t) {
+                    for (int t = 0; t < kQTiles; ++t) {
+                        if (!(ok = warp_wait(p_full0 + 8 * t, g & 1u, ctl, kSiteMmaV + 1 + t))) break;
+                        tc_fence_after();
+                        if (leader) {
 #pragma unroll
                             for (int kk = 0; kk < kBN / 16; ++kk)  // 16 KV rows: 8 TMEM columns of P, 16 x 128 B of V
                                 umma_ts_lo(tmem + 2 * kBN + 2 * kD + t * kD, tmem + 2 * kBN + t * kD + kk * 8,
                                            v_lo + kk * 128, desc_hi, kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
                             umma_commit(pv_done0 + 8 * t);
                         }
-                        umma_commit(v_empty0 + 8 * st);
+                        __syncwarp();
                     }
+                    if (!ok) break;
+                    if (leader) umma_commit(v_empty0 + 8 * st);
                     __syncwarp();
                     BF_TRACE(2, g, 3);
                 }

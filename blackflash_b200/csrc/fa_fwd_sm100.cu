@@ -6,15 +6,17 @@
 // fp32 accumulation. The reference's row-max / logsumexp slots
 // (include/flash_attn.cuh:27-28, never written there) are filled here.
 //
-// Persistent kernel: one CTA per SM (384 threads) walks work items
+// Persistent kernel: one CTA per SM (608 threads) walks work items
 // item = blockIdx.x + k * gridDim.x; an item is two 128-row query tiles
 // (256 rows) of one (b, h) slice against all of its KV rows. Roles:
-//   * warps 0-3 / 4-7: softmax warpgroups for query tile 0 / 1. One thread
-//     owns one query row (= one TMEM lane), so row max / row sum need no
-//     shuffles. They also rescale O in TMEM (lazily) and run the epilogue;
-//   * warp 8: TMA producer: Q (double-buffered across items) and K / V per
+//   * warps 0-7 / 8-15: softmax for query tile 0 / 1, four warps per
+//     scheduler. Each warp covers 16 rows (TMEM lanes); two threads of the
+//     warp share a row, one per 64-column half of S (tcgen05 16x32bx2
+//     shapes), so the row max takes one shuffle. They also rescale O in TMEM
+//     (lazily) and run the epilogue;
+//   * warp 16: TMA producer: Q (double-buffered across items) and K / V per
 //     128-row KV tile into a kStages-deep mbarrier ring, 128-byte swizzle;
-//   * warps 9 / 10: issue the tcgen05.mma streams (S / PV), warp 9 owns TMEM:
+//   * warps 17 / 18: issue the tcgen05.mma streams (S / PV), warp 17 owns TMEM:
 //       S_t = Q_t K_j^T   (M=128, N=128, K=64; A,B from smem)      -> TMEM
 //       O_t += P_t V_j    (M=128, N=64,  K=128; A=P from TMEM, B=V) -> TMEM
 //     P_t is written by the softmax threads as bf16 into its own TMEM
@@ -54,22 +56,18 @@ constexpr int kBM = 128;        // query rows per tile
 constexpr int kBN = 128;        // KV rows per tile
 constexpr int kQTiles = 2;      // query tiles per work item
 constexpr int kStages = 3;      // K/V ring depth
-constexpr int kThreads = 384;
+constexpr int kSoftWarps = 16;                       // 8 per query tile, 4 per scheduler
+constexpr int kThreads = kSoftWarps * 32 + 3 * 32;   // + TMA producer, S issuer, PV issuer
 constexpr int kTileBytes = kBM * kD * 2;  // 16 KiB (Q, K, V or O tile, bf16)
 constexpr int kTmemCols = 512;
-constexpr int kProducerWarp = 8;  // TMA producer
-constexpr int kSWarp = 9;         // issues S = Q K^T; owns the TMEM allocation
-constexpr int kPVWarp = 10;       // issues O += P V
-#ifndef BF_PINGPONG
-#define BF_PINGPONG 0
+constexpr int kProducerWarp = 16;  // TMA producer
+constexpr int kSWarp = 17;         // issues S = Q K^T; owns the TMEM allocation
+constexpr int kPVWarp = 18;        // issues O += P V
+#ifdef BF_PERF_DECOUPLE
+constexpr bool kPerfDecouple = true;  // perf experiment only: MMA and softmax do not wait on each other
+#else
+constexpr bool kPerfDecouple = false;
 #endif
-// Ping-pong (off by default: measured 2 % slower than free-running warpgroups
-// on B200, kept as a build option): the two softmax warpgroups take turns for their exponential phase
-// (warpgroup 0 of step g, then warpgroup 1 of step g, then warpgroup 0 of step
-// g+1, ...). Each one's exponentials then run with MUFU to itself while the
-// other loads S, reduces the max and stores P, instead of both fighting over
-// MUFU at the same time and leaving it idle together.
-constexpr bool kPingPong = BF_PINGPONG != 0;
 #ifndef BF_EMU_PAIRS
 #define BF_EMU_PAIRS 2
 #endif
@@ -93,7 +91,6 @@ struct Bars {
     uint64_t s_empty[kQTiles];
     uint64_t p_full[kQTiles];
     uint64_t pv_done[kQTiles];
-    uint64_t exp_turn[kQTiles];  // ping-pong: warpgroup t may start its exponentials
     uint64_t drain;
     uint64_t drain_pv;
     uint32_t tmem_base;
@@ -113,7 +110,6 @@ enum : unsigned {
     kSiteSoftS = 0x301,
     kSiteSoftO = 0x302,
     kSiteSoftPV = 0x303,
-    kSiteSoftTurn = 0x304,
 };
 
 struct KParams {
@@ -176,10 +172,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int t = 0; t < kQTiles; ++t) {
             mbar_init(smem_addr(&bars->s_full[t]), 1);
-            mbar_init(smem_addr(&bars->s_empty[t]), kBM);
-            mbar_init(smem_addr(&bars->p_full[t]), kBM);
+            mbar_init(smem_addr(&bars->s_empty[t]), 2 * kBM);
+            mbar_init(smem_addr(&bars->p_full[t]), 2 * kBM);
             mbar_init(smem_addr(&bars->pv_done[t]), 1);
-            mbar_init(smem_addr(&bars->exp_turn[t]), kBM);
         }
         mbar_init(smem_addr(&bars->drain), 1);
         mbar_init(smem_addr(&bars->drain_pv), 1);
@@ -202,19 +197,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = bars->tmem_base;
     const WaitCtl ctl{&bars->abort_flag, &g_wait_status, p.timeout_ns};
 
-    // Launch budget is 168 regs x 384 threads; give the softmax warpgroups
-    // 216 each (they hold a 128-column S row) and the TMA/MMA warpgroup 72:
-    // 216*256 + 72*128 = 64512 = 168*384.
-    if (warp < 8)
-        regs_inc<216>();
-    else
-        regs_dec<72>();
-
-    if (warp < 8) {
+    if (warp < kSoftWarps) {
         // ------------------------------------------------------------ softmax
-        const int t = warp >> 2;                 // query tile of this warpgroup
-        const int row = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
-        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        // Tile t has 8 warps. Warp w covers 16 TMEM lanes (rows) of its lane
+        // quarter (w % 4); within the warp, lanes i and i + 16 share a row,
+        // lane i < 16 holding S columns [0, 64) and lane i + 16 columns [64, 128)
+        // (tcgen05 16x32bx2 shapes). The row max needs one shuffle; the row
+        // sum stays per half and is combined in the epilogue.
+        const int t = warp >> 3;
+        const int quarter = warp & 3;
+        const int sub = (warp >> 2) & 1;
+        const int h = lane >> 4;  // column half
+        const int row = quarter * 32 + sub * 16 + (lane & 15);  // row within the tile == TMEM lane
+        const uint32_t lane_off = (uint32_t)(quarter * 32 + sub * 16) << 16;
         const uint32_t tS = tmem + lane_off + (uint32_t)(t * kBN);
         const uint32_t tP = tmem + lane_off + (uint32_t)(2 * kBN + t * kD);
         const uint32_t tO = tmem + lane_off + (uint32_t)(2 * kBN + 2 * kD + t * kD);
@@ -224,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t bar_se = smem_addr(&bars->s_empty[t]);
         const uint32_t bar_p = smem_addr(&bars->p_full[t]);
         const uint32_t bar_pv = smem_addr(&bars->pv_done[t]);
-        const bool issuer = (warp & 3) == 0 && lane == 0;  // issues this warpgroup's TMA stores
+        const bool issuer = (warp & 7) == 0 && lane == 0;  // issues tile t's TMA stores
         const bool tracing = trace_hit && issuer;
         uint8_t* stage = smem + kOffO + t * kTileBytes;
         uint32_t g = 0;  // global KV step of this CTA
@@ -235,19 +230,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int q_row0 = (item % p.q_blocks) * (kQTiles * kBM);
             float m_use = -INFINITY;  // reference max (log2 domain) the current P/O/l are relative to
             float m_raw = -INFINITY;  // true running max of raw scores
-            float l_sum = 0.f;
+            float l_half = 0.f;       // row sum over this thread's column half
 
             for (int j = 0; j < nk; ++j, ++g) {
                 BF_TRACE(t, g, 0);
-                if (!(ok = warp_wait(bar_s, g & 1u, ctl, kSiteSoftS))) break;
+                if (!kPerfDecouple && !(ok = warp_wait(bar_s, g & 1u, ctl, kSiteSoftS))) break;
                 tc_fence_after();
                 BF_TRACE(t, g, 1);
 
-                uint32_t s[4][32];
-                tmem_ld32(tS + 0, s[0]);
-                tmem_ld32(tS + 32, s[1]);
-                tmem_ld32(tS + 64, s[2]);
-                tmem_ld32(tS + 96, s[3]);
+                uint32_t s[2][32];  // columns 64h + [0, 32) and 64h + [32, 64)
+                tmem_ld16x32bx2_x32<64>(tS + 0, s[0]);
+                tmem_ld16x32bx2_x32<64>(tS + 32, s[1]);
                 tmem_wait_ld();
                 tc_fence_before();
                 mbar_arrive(bar_se);  // S_t may now be overwritten by the next step's S_t
@@ -255,25 +248,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
                 if (p.dbg_s != nullptr && item == 0 && t == 0 && j == 0) {
 #pragma unroll
-                    for (int c = 0; c < kBN; ++c) p.dbg_s[row * kBN + c] = __uint_as_float(s[c >> 5][c & 31]);
+                    for (int c = 0; c < 64; ++c) p.dbg_s[row * kBN + h * 64 + c] = __uint_as_float(s[c >> 5][c & 31]);
                 }
 
-                const int valid = p.n_kv - j * kBN;  // >= 1
-                if (valid < kBN) {
+                const int valid = p.n_kv - j * kBN - h * 64;  // may be <= 0 on the ragged last tile
+                if (valid < 64) {
 #pragma unroll
-                    for (int c = 0; c < kBN; ++c)
+                    for (int c = 0; c < 64; ++c)
                         if (c >= valid) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
                 }
 
-                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+                float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
                     mx0 = fmax3(mx0, __uint_as_float(s[0][c]), __uint_as_float(s[0][c + 1]));
                     mx1 = fmax3(mx1, __uint_as_float(s[1][c]), __uint_as_float(s[1][c + 1]));
-                    mx2 = fmax3(mx2, __uint_as_float(s[2][c]), __uint_as_float(s[2][c + 1]));
-                    mx3 = fmax3(mx3, __uint_as_float(s[3][c]), __uint_as_float(s[3][c + 1]));
                 }
-                const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+                float mx = fmaxf(mx0, mx1);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));  // the row's other half
                 m_raw = fmaxf(m_raw, mx);
                 const float m_new = mx * sl2;
                 BF_TRACE(t, g, 3);
@@ -286,22 +278,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     alpha = fast_exp2(m_use - m_new);  // 0 on the first tile
                     m_use = m_new;
                 }
-                l_sum *= alpha;
+                l_half *= alpha;
 
-                if (kPingPong && (t == 1 || g > 0)) {
-                    const uint32_t turn_par = t == 0 ? ((g - 1) & 1u) : (g & 1u);
-                    if (!(ok = warp_wait(smem_addr(&bars->exp_turn[t]), turn_par, ctl, kSiteSoftTurn))) break;
-                }
                 const uint64_t negm_2 = f2_pack(-m_use, -m_use);
                 uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = f2_pack(0.f, 0.f);
-                uint32_t pk[4][16];
+                uint32_t pk[2][16];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < 2; ++q) {
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
                         const uint64_t x2 = f2_fma(
                             f2_pack(__uint_as_float(s[q][2 * c]), __uint_as_float(s[q][2 * c + 1])), sl2_2, negm_2);
                         uint64_t p2;
+#ifdef BF_PERF_NO_EXP
+                        if (true) {
+                            p2 = x2;  // perf experiment only: exponentials skipped, results are wrong
+                        } else
+#endif
                         if ((c & 7) < kEmuPairs) {
                             p2 = exp2_poly_x2(x2);
                         } else {
@@ -322,31 +315,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float a0, a1, b0, b1;
                     f2_unpack(sum_a, a0, a1);
                     f2_unpack(sum_b, b0, b1);
-                    l_sum += (a0 + a1) + (b0 + b1);
+                    l_half += (a0 + a1) + (b0 + b1);
                 }
-                if (kPingPong) mbar_arrive(smem_addr(&bars->exp_turn[1 - t]));  // hand MUFU to the other warpgroup
                 BF_TRACE(t, g, 4);
 
                 // P_t of the previous step must have been consumed (and O_t be final)
                 // before we overwrite P_t / rescale O_t.
-                if (g > 0) {
+                if (g > 0 && !kPerfDecouple) {
                     if (!(ok = warp_wait(bar_pv, (g - 1) & 1u, ctl, kSiteSoftPV))) break;
                     tc_fence_after();
                 }
                 BF_TRACE(t, g, 5);
                 if (j > 0 && __any_sync(0xffffffffu, need)) {
-                    uint32_t o[32];
+                    uint32_t o[32];  // O columns 32h + [0, 32)
+                    tmem_ld16x32bx2_x32<32>(tO, o);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        tmem_ld32(tO + h * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                        tmem_st32(tO + h * 32, o);
-                    }
+                    for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                    tmem_st16x32bx2_x32<32>(tO, o);
                 }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) tmem_st16(tP + q * 16, pk[q]);
+                // bf16 P: this thread's 64 S columns are P columns 32h + [0, 32).
+                tmem_st16x32bx2_x16<32>(tP, pk[0]);
+                tmem_st16x32bx2_x16<32>(tP + 16, pk[1]);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(bar_p);
@@ -355,48 +345,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
 
             // ---------------------------------------------------- epilogue of this item
-            if (!(ok = warp_wait(bar_pv, (g - 1) & 1u, ctl, kSiteSoftO))) break;
+            if (!kPerfDecouple && !(ok = warp_wait(bar_pv, (g - 1) & 1u, ctl, kSiteSoftO))) break;
             tc_fence_after();
-            uint32_t o[2][32];
-            tmem_ld32(tO, o[0]);
-            tmem_ld32(tO + 32, o[1]);
+            uint32_t o[32];
+            tmem_ld16x32bx2_x32<32>(tO, o);
             tmem_wait_ld();
+            const float l_sum = l_half + __shfl_xor_sync(0xffffffffu, l_half, 16);
             const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
             const int q_row = q_row0 + t * kBM + row;
             const bool row_ok = q_row < p.n_q;
 
             if constexpr (kF32Out) {
                 if (row_ok) {
-                    float4* dst = reinterpret_cast<float4*>(p.o_f32 + ((size_t)bh * p.n_q + q_row) * kD);
+                    float4* dst = reinterpret_cast<float4*>(p.o_f32 + ((size_t)bh * p.n_q + q_row) * kD + h * 32);
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        const uint32_t* src = &o[c >> 3][(c & 7) * 4];
-                        dst[c] = make_float4(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv,
-                                             __uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-                    }
+                    for (int c = 0; c < 8; ++c)
+                        dst[c] = make_float4(__uint_as_float(o[4 * c]) * inv, __uint_as_float(o[4 * c + 1]) * inv,
+                                             __uint_as_float(o[4 * c + 2]) * inv, __uint_as_float(o[4 * c + 3]) * inv);
                 }
             } else {
                 // bf16 tile in the 128-byte-swizzled image the O tensor map expects, then TMA store.
                 if (issuer) tma_store_wait_read0();  // the previous item's store has left the staging buffer
-                named_bar_sync(1 + t, 128);
+                named_bar_sync(1 + t, 2 * kBM);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint32_t* src = &o[c >> 2][(c & 3) * 8];
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t* src = &o[c * 8];
                     uint4 v;
                     v.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
                     v.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
                     v.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
                     v.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-                    *reinterpret_cast<uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4)) = v;
+                    const int chunk = h * 4 + c;
+                    *reinterpret_cast<uint4*>(stage + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
                 }
                 fence_proxy_async_smem();
-                named_bar_sync(1 + t, 128);
+                named_bar_sync(1 + t, 2 * kBM);
                 if (issuer) {
                     tma_store_3d(&tmO, smem_addr(stage), 0, q_row0 + t * kBM, bh);
                     tma_store_commit();
                 }
             }
-            if (row_ok) {
+            if (row_ok && h == 0) {
                 const size_t idx = (size_t)bh * p.n_q + q_row;
                 if (p.lse) p.lse[idx] = (m_use + __log2f(l_sum)) * 0.69314718055994531f;
                 if (p.row_max) p.row_max[idx] = m_raw * p.scale;
@@ -512,10 +501,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t k_lo = k_lo0 + (uint32_t)st * kTileLo;
 #pragma unroll
                     for (int t = 0; t < kQTiles; ++t) {
-                        if (g > 0) {
+                        if (g > 0 && !kPerfDecouple) {
                             if (!(ok = warp_wait(s_empty0 + 8 * t, (g - 1) & 1u, ctl, kSiteMmaK + 1 + t))) break;
                             tc_fence_after();
                         }
+                        BF_TRACE(2, g, 4 + t);  // S_t(g) issue starts
                         if (leader) {
                             const uint32_t q_lo = q_lo0 + (uint32_t)(qb * kQTiles + t) * kTileLo;
 #pragma unroll
@@ -539,8 +529,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t v_lo = v_lo0 + (uint32_t)st * kTileLo;
 #pragma unroll
                     for (int t = 0; t < kQTiles; ++t) {
-                        if (!(ok = warp_wait(p_full0 + 8 * t, g & 1u, ctl, kSiteMmaV + 1 + t))) break;
+                        if (!kPerfDecouple && !(ok = warp_wait(p_full0 + 8 * t, g & 1u, ctl, kSiteMmaV + 1 + t))) break;
                         tc_fence_after();
+                        BF_TRACE(2, g, 6 + t);  // PV_t(g) issue starts
                         if (leader) {
 #pragma unroll
                             for (int kk = 0; kk < kBN / 16; ++kk)  // 16 KV rows: 8 TMEM columns of P, 16 x 128 B of V

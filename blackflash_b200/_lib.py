@@ -16,6 +16,7 @@ BF_OK, BF_ERR_ARG, BF_ERR_CUDA, BF_ERR_TIMEOUT = 0, 1, 2, 3
 # Every symbol the header declares (checked by the CPU test suite).
 EXPORTED = (
     "blackflash_fwd",
+    "blackflash_fwd_causal",
     "blackflash_fwd_partial",
     "blackflash_lse_merge",
     "blackflash_f32_to_bf16",
@@ -34,6 +35,7 @@ _vp, _fp, _i, _ll, _f = ctypes.c_void_p, ctypes.POINTER(ctypes.c_float), ctypes.
 
 _SIGS = {
     "blackflash_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp]),
+    "blackflash_fwd_causal": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp]),
     "blackflash_fwd_partial": (_i, [_vp, _vp, _vp, _vp, _vp, _ll, _i, _i, _i, _f, _vp]),
     "blackflash_lse_merge": (_i, [_vp, _vp, _vp, _vp, _ll, _i, _vp]),
     "blackflash_f32_to_bf16": (_i, [_vp, _vp, _ll, _vp]),

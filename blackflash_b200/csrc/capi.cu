@@ -52,6 +52,18 @@ extern "C" int blackflash_fwd(const void* Q, const void* K, const void* V, void*
     return bf_fwd_launch(&a);
 }
 
+extern "C" int blackflash_fwd_causal(const void* Q, const void* K, const void* V, void* O, float* lse,
+                                     float* row_max, int B, int H, int N, int d, float scale, void* stream) {
+    g_last_error[0] = 0;
+    if (check_bhn(B, H, N) != BF_OK) return BF_ERR_ARG;
+    BfFwdArgs a = base_args(Q, K, V, B, H, N, d, scale, stream);
+    a.o = O;
+    a.lse = lse;
+    a.row_max = row_max;
+    a.causal = 1;
+    return bf_fwd_launch(&a);
+}
+
 extern "C" int blackflash_fwd_partial(const void* Q, const void* K, const void* V, float* O_f32, float* lse,
                                       long long BH, int Nq, int Nkv, int d, float scale, void* stream) {
     g_last_error[0] = 0;

@@ -125,6 +125,7 @@ struct KParams {
     unsigned long long timeout_ns;
     float* dbg_s;   // optional: raw S of (item 0, tile 0, KV tile 0), 128x128 fp32
     int skip_k_loads;  // test hook: producer never loads K (forces a wait timeout)
+    int causal;        // key j visible to query i only if j <= i (top-left aligned)
     long long* trace;  // kTrace builds: clock64 event stamps of CTA `trace_cta`
     int trace_cta;
 };
@@ -142,6 +143,23 @@ struct KParams {
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Work item -> (slice, first query row). With the causal mask the late query
+// blocks carry the most KV tiles, so they are handed out first.
+__device__ __forceinline__ void decode_item(const KParams& p, int item, int& bh, int& q_row0) {
+    bh = item / p.q_blocks;
+    int qb = item % p.q_blocks;
+    if (p.causal) qb = p.q_blocks - 1 - qb;
+    q_row0 = qb * (kQTiles * kBM);
+}
+
+// KV tiles an item visits: all of them, or with the causal mask those up to the
+// item's last query row (the diagonal tiles are masked element-wise).
+__device__ __forceinline__ int item_kv_tiles(const KParams& p, int q_row0, int nk) {
+    if (!p.causal) return nk;
+    const int last_row = min(q_row0 + kQTiles * kBM, p.n_q) - 1;
+    return min(last_row / kBN + 1, nk);
 }
 
 template <bool kF32Out, bool kTrace = false>
@@ -226,13 +244,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
 
         for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-            const int bh = item / p.q_blocks;
-            const int q_row0 = (item % p.q_blocks) * (kQTiles * kBM);
+            int bh, q_row0;
+            decode_item(p, item, bh, q_row0);
+            const int nk_item = item_kv_tiles(p, q_row0, nk);
             float m_use = -INFINITY;  // reference max (log2 domain) the current P/O/l are relative to
             float m_raw = -INFINITY;  // true running max of raw scores
             float l_half = 0.f;       // row sum over this thread's column half
 
-            for (int j = 0; j < nk; ++j, ++g) {
+            for (int j = 0; j < nk_item; ++j, ++g) {
                 BF_TRACE(t, g, 0);
                 if (!kPerfDecouple && !(ok = warp_wait(bar_s, g & 1u, ctl, kSiteSoftS))) break;
                 tc_fence_after();
@@ -251,7 +270,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int c = 0; c < 64; ++c) p.dbg_s[row * kBN + h * 64 + c] = __uint_as_float(s[c >> 5][c & 31]);
                 }
 
-                const int valid = p.n_kv - j * kBN - h * 64;  // may be <= 0 on the ragged last tile
+                // Visible keys of this row, relative to this thread's first column
+                // (may be <= 0: ragged last tile or, with the causal mask, past the diagonal).
+                const int q_abs = q_row0 + t * kBM + row;
+                const int kv_lim = p.causal ? min(p.n_kv, q_abs + 1) : p.n_kv;
+                const int valid = kv_lim - j * kBN - h * 64;
                 if (valid < 64) {
 #pragma unroll
                     for (int c = 0; c < 64; ++c)
@@ -411,8 +434,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         int it = 0;
         for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++it) {
-            const int bh = item / p.q_blocks;
-            const int q_row0 = (item % p.q_blocks) * (kQTiles * kBM);
+            int bh, q_row0;
+            decode_item(p, item, bh, q_row0);
+            const int nk_item = item_kv_tiles(p, q_row0, nk);
             const int qb = it & 1;
             if (!(ok = warp_wait(q_empty0 + 8 * qb, (uint32_t)((it >> 1) & 1) ^ 1u, ctl, kSiteProdQEmpty))) break;
             if (leader) {
@@ -423,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             last_q = it;
             __syncwarp();
-            for (int j = 0; j < nk; ++j, ++c) {
+            for (int j = 0; j < nk_item; ++j, ++c) {
                 if (!(ok = warp_wait(k_empty0 + 8 * st, par, ctl, kSiteProdKEmpty))) break;
                 if (!p.skip_k_loads) {
                     if (leader) {
@@ -487,11 +511,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         int it = 0;
         for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++it) {
             const int qb = it & 1;
+            int bh_unused, q_row0;
+            decode_item(p, item, bh_unused, q_row0);
+            const int nk_item = item_kv_tiles(p, q_row0, nk);
             if (is_s) {
                 if (!(ok = warp_wait(q_full0 + 8 * qb, (uint32_t)(it >> 1) & 1u, ctl, kSiteMmaQ))) break;
                 tc_fence_after();
             }
-            for (int j = 0; j < nk; ++j, ++g) {
+            for (int j = 0; j < nk_item; ++j, ++g) {
                 if (is_s) {
                     // K(g) loaded; then each S_t is issued as soon as its softmax has read S_t(g-1),
                     // so the two tiles may run half a step apart (ping-pong).
@@ -518,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok) break;
                     if (leader) {
                         umma_commit(k_empty0 + 8 * st);
-                        if (j == nk - 1) umma_commit(q_empty0 + 8 * qb);  // last S of this item: Q buffer free
+                        if (j == nk_item - 1) umma_commit(q_empty0 + 8 * qb);  // last S of this item: Q buffer free
                     }
                     __syncwarp();
                     BF_TRACE(2, g, 1);
@@ -678,6 +705,7 @@ int bf_fwd_launch(const BfFwdArgs* a) {
     kp.dbg_s = a->dbg_s;
     kp.skip_k_loads = a->skip_k_loads;
     kp.trace = a->trace;
+    kp.causal = a->causal;
     kp.trace_cta = a->trace_cta;
 
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(a->stream);

@@ -23,6 +23,7 @@ struct BfFwdArgs {
     int skip_k_loads;
     long long* trace;
     int trace_cta;
+    int causal;  // 1: key j visible to query i only if j <= i
 };
 
 int bf_fwd_launch(const BfFwdArgs* a);

@@ -44,8 +44,12 @@ def forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float) -> 
     return forward_lse(Q, K, V, scale, want_stats=False)[0]
 
 
-def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float, want_stats: bool = True):
+def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float, want_stats: bool = True,
+                causal: bool = False):
     """Like `forward`, and also returns (lse, row_max), each fp32 [B, H, N].
+
+    causal=True applies a causal mask (query i sees keys j <= i); the reference
+    has no causal kernel, so this is an extension (its default is off).
 
     lse[b,h,i] = log sum_j exp(scale * S_ij) and row_max[b,h,i] = max_j scale * S_ij:
     the two quantities the reference's l/m slots were declared for
@@ -61,20 +65,25 @@ def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float,
     if Q.numel() == 0:
         return O, lse, m
     lib = _lib.load()
+    fn = lib.blackflash_fwd_causal if causal else lib.blackflash_fwd
     with torch.cuda.device(Q.device):
-        rc = lib.blackflash_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
-                                lse.data_ptr() if lse is not None else None,
-                                m.data_ptr() if m is not None else None,
-                                B, H, N, d, float(scale), _stream_handle(Q.device))
-    _lib.check(rc, "blackflash_fwd")
+        rc = fn(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                lse.data_ptr() if lse is not None else None,
+                m.data_ptr() if m is not None else None,
+                B, H, N, d, float(scale), _stream_handle(Q.device))
+    _lib.check(rc, "blackflash_fwd_causal" if causal else "blackflash_fwd")
     return O, lse, m
 
 
-def blackflash(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+def blackflash(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float | None = None,
+               causal: bool = False) -> torch.Tensor:
     """Attention forward. Mirrors the reference's Python API (blackflash/__init__.py:5-18):
-    Q, K, V are [B, H, N, d] bf16 CUDA tensors with d == 64; scale defaults to 1/sqrt(d)."""
+    Q, K, V are [B, H, N, d] bf16 CUDA tensors with d == 64; scale defaults to 1/sqrt(d).
+    `causal` (default False, the reference's only mode) is an extension."""
     if scale is None:
         scale = 1.0 / math.sqrt(Q.size(-1))
+    if causal:
+        return forward_lse(Q, K, V, scale, want_stats=False, causal=True)[0]
     return forward(Q, K, V, scale)
 
 

@@ -42,6 +42,16 @@ int blackflash_fwd(const void* Q, const void* K, const void* V, void* O, float* 
                    int N, int d, float scale, void* stream);
 
 /*
+ * blackflash_fwd with a causal mask: query i attends to keys j <= i (top-left
+ * aligned, Q and K of the same length N). Tiles above the diagonal are skipped,
+ * so the work is about half. lse / row_max are taken over the visible keys. No
+ * counterpart in the reference kernel (non-causal only); its benchmark times the
+ * causal case with cuDNN (tests/bench_blackflash.py:58-60).
+ */
+int blackflash_fwd_causal(const void* Q, const void* K, const void* V, void* O, float* lse, float* row_max, int B,
+                          int H, int N, int d, float scale, void* stream);
+
+/*
  * Partial attention of one query block against one KV block. It is the
  * per-step kernel of the ring (sequence-parallel) mode and has no counterpart
  * in the reference.

@@ -22,6 +22,8 @@
  *                     throughout, as on the GPU. Like the reference, it assumes
  *                     N % 64 == 0 (no tail masking).
  *
+ *  oracle_attn_exact_causal  the same with a causal mask (key j visible to query i iff j <= i).
+ *
  *  oracle_scores      S and P = softmax(S) of one slice in fp32, the quantities
  *                     gen_ref.py saves as s_ref.bin / p_ref.bin (:80-84, :183-184).
  *
@@ -59,6 +61,7 @@ typedef struct {
     int nq, nkv, d;
     float scale;
     int mode; /* 0 exact, 1 fa2 */
+    int causal; /* exact mode: key j is visible to query i only if j <= i */
 } Job;
 
 static void exact_slice(const Job* j, long long s) {
@@ -78,7 +81,8 @@ static void exact_slice(const Job* j, long long s) {
     for (int i = 0; i < nq; ++i) {
         for (int c = 0; c < d; ++c) qf[c] = bf16_to_f32(q[(size_t)i * d + c]);
         double mx = -INFINITY;
-        for (int jj = 0; jj < nkv; ++jj) {
+        const int lim = j->causal ? (i + 1 < nkv ? i + 1 : nkv) : nkv;
+        for (int jj = 0; jj < lim; ++jj) {
             double dot = 0.0;
             const float* kr = kf + (size_t)jj * d;
             for (int c = 0; c < d; ++c) dot += (double)qf[c] * (double)kr[c];
@@ -87,7 +91,7 @@ static void exact_slice(const Job* j, long long s) {
         }
         double sum = 0.0;
         for (int c = 0; c < d; ++c) acc[c] = 0.0;
-        for (int jj = 0; jj < nkv; ++jj) {
+        for (int jj = 0; jj < lim; ++jj) {
             const double p = exp(srow[jj] - mx);
             sum += p;
             const float* vr = vf + (size_t)jj * d;
@@ -182,8 +186,19 @@ static int run(Job base, long long bh, int nthreads) {
     return 0;
 }
 
+int oracle_attn_exact_causal(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* o, float* lse,
+                             float* rowmax, long long bh, int nq, int nkv, int d, float scale, int causal, int nthreads);
+
 int oracle_attn_exact(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* o, float* lse, float* rowmax,
                       long long bh, int nq, int nkv, int d, float scale, int nthreads) {
+    return oracle_attn_exact_causal(q, k, v, o, lse, rowmax, bh, nq, nkv, d, scale, 0, nthreads);
+}
+
+/* Causal variant (key j visible to query i iff j <= i, top-left aligned). This is
+ * not a reference feature. The reference is non-causal only, and its benchmark
+ * times cuDNN with is_causal=True (tests/bench_blackflash.py:58-60). */
+int oracle_attn_exact_causal(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* o, float* lse,
+                             float* rowmax, long long bh, int nq, int nkv, int d, float scale, int causal, int nthreads) {
     Job b;
     memset(&b, 0, sizeof(b));
     b.q = q;
@@ -197,6 +212,7 @@ int oracle_attn_exact(const uint16_t* q, const uint16_t* k, const uint16_t* v, f
     b.d = d;
     b.scale = scale;
     b.mode = 0;
+    b.causal = causal;
     return run(b, bh, nthreads);
 }
 

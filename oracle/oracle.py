@@ -42,6 +42,8 @@ def _load():
         lib = ctypes.CDLL(build())
         vp, ll, i, f = ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_float
         lib.oracle_attn_exact.argtypes = [vp, vp, vp, vp, vp, vp, ll, i, i, i, f, i]
+        lib.oracle_attn_exact_causal.argtypes = [vp, vp, vp, vp, vp, vp, ll, i, i, i, f, i, i]
+        lib.oracle_attn_exact_causal.restype = i
         lib.oracle_attn_fa2.argtypes = [vp, vp, vp, vp, vp, vp, ll, i, i, f, i]
         lib.oracle_scores.argtypes = [vp, vp, vp, vp, i, i, f]
         for fn in (lib.oracle_attn_exact, lib.oracle_attn_fa2, lib.oracle_scores):
@@ -72,8 +74,9 @@ def _ptr(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
-def attn_exact(q, k, v, scale: float, nthreads: int | None = None):
-    """q: [..., Nq, d], k/v: [..., Nkv, d] bf16. Returns (O, lse, rowmax) fp32 numpy."""
+def attn_exact(q, k, v, scale: float, nthreads: int | None = None, causal: bool = False):
+    """q: [..., Nq, d], k/v: [..., Nkv, d] bf16. Returns (O, lse, rowmax) fp32 numpy.
+    causal=True masks key j for query i when j > i."""
     qb, kb, vb = as_bf16_bits(q), as_bf16_bits(k), as_bf16_bits(v)
     *lead, nq, d = qb.shape
     nkv = kb.shape[-2]
@@ -81,8 +84,8 @@ def attn_exact(q, k, v, scale: float, nthreads: int | None = None):
     o = np.empty(qb.shape, dtype=np.float32)
     lse = np.empty((*lead, nq), dtype=np.float32)
     mx = np.empty((*lead, nq), dtype=np.float32)
-    _load().oracle_attn_exact(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(o), _ptr(lse), _ptr(mx), bh, nq, nkv, d,
-                              float(scale), nthreads or os.cpu_count() or 1)
+    _load().oracle_attn_exact_causal(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(o), _ptr(lse), _ptr(mx), bh, nq, nkv, d,
+                                     float(scale), 1 if causal else 0, nthreads or os.cpu_count() or 1)
     return o, lse, mx
 
 
@@ -109,12 +112,15 @@ def scores(q_slice, k_slice, scale: float):
     return s, p
 
 
-def attn_numpy(q, k, v, scale: float):
+def attn_numpy(q, k, v, scale: float, causal: bool = False):
     """float64 numpy math attention on bf16 inputs; returns (O, lse) float64."""
     qf = bf16_bits_to_f32(as_bf16_bits(q)).astype(np.float64)
     kf = bf16_bits_to_f32(as_bf16_bits(k)).astype(np.float64)
     vf = bf16_bits_to_f32(as_bf16_bits(v)).astype(np.float64)
     s = np.einsum("...id,...jd->...ij", qf, kf) * scale
+    if causal:
+        nq, nk = s.shape[-2], s.shape[-1]
+        s = np.where(np.arange(nk)[None, :] <= np.arange(nq)[:, None], s, -np.inf)
     m = s.max(axis=-1, keepdims=True)
     e = np.exp(s - m)
     den = e.sum(axis=-1, keepdims=True)

@@ -74,3 +74,13 @@ def test_torch_math_matches_exact():
     o = oracle.torch_math(q, k, v, 0.125).numpy()
     o2, _, _ = oracle.attn_exact(q, k, v, 0.125)
     np.testing.assert_allclose(o, o2, atol=2e-6)
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 37, 64), (2, 1, 300, 64), (1, 1, 1, 64)])
+def test_causal_exact_vs_numpy(shape):
+    from blackflash_b200.inputs import make_qkv
+    q, k, v = make_qkv(*shape, dist="peaked", seed=11)
+    o, lse, _ = oracle.attn_exact(q, k, v, 0.125, causal=True)
+    o64, lse64 = oracle.attn_numpy(q, k, v, 0.125, causal=True)
+    np.testing.assert_allclose(o, o64, atol=1e-6, rtol=1e-6)
+    np.testing.assert_allclose(lse, lse64, atol=1e-5)

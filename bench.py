@@ -10,8 +10,9 @@ the ranks with no collective (strong scaling: total work fixed).
 
 One step = one kernel launch over this rank's slices, inputs resident in HBM.
 `value` = total FLOPs of all ranks / max-over-ranks device time.
-`e2e`   = the same metric through the public API (blackflash_b200.blackflash)
-          with Q/K/V copied from pinned host memory and O copied back each step.
+`e2e`   = the same metric through the public host-buffer API (blackflash_b200.blackflash_host):
+          Q/K/V in pinned host memory, O returned in host memory, every step; the
+          copies of one slice group overlap the kernel of the previous one.
 `--impl reference` times the reference's CPU path (torch fp32 math attention,
 reference tests/test_blackflash.py:16-19) on the host cores, rank 0 only.
 
@@ -193,7 +194,7 @@ def run_reference(args, cfg_name):
 def run_ours(args, cfg_name):
     import torch.distributed as dist_mod
 
-    from blackflash_b200 import _lib, blackflash
+    from blackflash_b200 import _lib
     from blackflash_b200.inputs import make_qkv
     from blackflash_b200.shard import slice_range
 
@@ -262,17 +263,15 @@ def run_ours(args, cfg_name):
     value = f_total / (ms_step * 1e-3) / 1e12
     clocks = sampler.summary(h0, h1)
 
-    # ---- end to end through the public API, host buffers (pinned) in and out
+    # ---- end to end through the public API with host buffers: blackflash_host takes pinned
+    # host Q/K/V and returns O in host memory, overlapping the copies with the kernel.
+    from blackflash_b200 import blackflash_host
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
     oh = torch.empty(O.shape, dtype=O.dtype, pin_memory=True)
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
 
     def e2e_step():
-        qd = qh.to(dev, non_blocking=True)
-        kd = kh.to(dev, non_blocking=True)
-        vd = vh.to(dev, non_blocking=True)
-        od = blackflash(qd, kd, vd, scale)
-        oh.copy_(od, non_blocking=True)
+        blackflash_host(qh, kh, vh, scale, device=dev, out=oh)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -281,7 +280,7 @@ def run_ours(args, cfg_name):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(e2e_steps):
-        e2e_step()
+        e2e_step()  # the caller's stream waits for the copies and the kernel of the call
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()

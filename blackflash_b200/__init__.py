@@ -6,9 +6,9 @@
 The compute path is libblackflash_b200.so (tcgen05 / TMA / TMEM kernel); there
 is no CPU fallback.
 """
-from .ops import (attention_partial, blackflash, forward, forward_lse, lse_merge_,  # noqa: F401
-                  to_bf16, wait_status)
+from .ops import (attention_partial, blackflash, blackflash_host, forward, forward_lse,  # noqa: F401
+                  lse_merge_, to_bf16, wait_status)
 from . import blackflash_cuda  # noqa: F401
 
-__all__ = ["blackflash", "forward", "forward_lse", "attention_partial", "lse_merge_", "to_bf16", "wait_status",
+__all__ = ["blackflash", "blackflash_host", "forward", "forward_lse", "attention_partial", "lse_merge_", "to_bf16", "wait_status",
            "blackflash_cuda"]

@@ -140,3 +140,66 @@ def wait_status(reset: bool = True) -> int:
     out = ctypes.c_uint(0)
     _lib.check(_lib.load().blackflash_status(1 if reset else 0, ctypes.byref(out)), "blackflash_status")
     return int(out.value)
+
+
+def blackflash_host(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float | None = None,
+                    causal: bool = False, device: torch.device | int | str = 0, chunks: int = 8,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention forward for Q, K, V held in (preferably pinned) host memory.
+
+    The (b, h) slices are processed in `chunks` groups on three CUDA streams, so the
+    host->device copy of group i+1, the kernel on group i and the device->host copy of
+    group i-1 run at the same time; the transfer, not the kernel, bounds the call.
+    Returns O in host memory (pinned, or `out` if given). Synchronous: O is ready when
+    the call returns.
+    """
+    for name, t in (("Q", Q), ("K", K), ("V", V)):
+        _require(not t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.dim() == 4,
+                 f"{name} must be a contiguous host bf16 [B, H, N, d] tensor")
+    _require(K.shape == Q.shape and V.shape == Q.shape, "Q, K and V must have the same shape")
+    _require(Q.size(3) == 64, "BlackFlash currently only supports d=64")
+    B, H, N, d = Q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+    if out is None:
+        out = torch.empty(Q.shape, dtype=Q.dtype, pin_memory=True)
+    _require(out.shape == Q.shape and out.dtype == Q.dtype and not out.is_cuda and out.is_contiguous(),
+             "out must be a contiguous host bf16 tensor of Q's shape")
+    S = B * H
+    if S == 0 or N == 0:
+        return out
+    qs, ks, vs, os_ = (t.view(S, 1, N, d) for t in (Q, K, V, out))
+    chunks = max(1, min(chunks, S))
+    lib = _lib.load()
+    bounds = [(S * i // chunks, S * (i + 1) // chunks) for i in range(chunks)]
+    with torch.cuda.device(dev):
+        dq, dk, dv = (torch.empty((S, 1, N, d), dtype=Q.dtype, device=dev) for _ in range(3))
+        do = torch.empty((S, 1, N, d), dtype=Q.dtype, device=dev)
+        h2d, comp, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        caller = torch.cuda.current_stream(dev)
+        for st in (h2d, comp, d2h):
+            st.wait_stream(caller)
+        for a, b in bounds:
+            if b == a:
+                continue
+            with torch.cuda.stream(h2d):
+                dq[a:b].copy_(qs[a:b], non_blocking=True)
+                dk[a:b].copy_(ks[a:b], non_blocking=True)
+                dv[a:b].copy_(vs[a:b], non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(h2d)
+            with torch.cuda.stream(comp):
+                comp.wait_event(ev_in)
+                fn = lib.blackflash_fwd_causal if causal else lib.blackflash_fwd
+                _lib.check(fn(dq[a:b].data_ptr(), dk[a:b].data_ptr(), dv[a:b].data_ptr(), do[a:b].data_ptr(),
+                              None, None, b - a, 1, N, d, float(scale), comp.cuda_stream), "blackflash_host")
+                ev_out = torch.cuda.Event()
+                ev_out.record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ev_out)
+                os_[a:b].copy_(do[a:b], non_blocking=True)
+        for st in (h2d, comp, d2h):
+            caller.wait_stream(st)
+        d2h.synchronize()
+    return out

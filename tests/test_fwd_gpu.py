@@ -181,3 +181,24 @@ def test_bounded_wait_timeout_reports_status():
     assert wait_status(reset=False) == 0
     # context still healthy: a normal call works and is correct
     _run_and_check(1, 2, 512, "normal", seed=1)
+
+
+@pytest.mark.parametrize("causal,chunks", [(False, 8), (True, 3), (False, 1)])
+def test_host_buffer_api_matches_device_api(causal, chunks):
+    """blackflash_host (pinned host tensors in and out, chunked and overlapped) equals the device API."""
+    from blackflash_b200 import blackflash, blackflash_host
+    from blackflash_b200.inputs import make_qkv
+    q, k, v = make_qkv(3, 5, 700, seed=17)
+    qh, kh, vh = (t.pin_memory() for t in (q, k, v))
+    O_host = blackflash_host(qh, kh, vh, causal=causal, chunks=chunks)
+    O_dev = blackflash(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+    torch.cuda.synchronize()
+    assert not O_host.is_cuda
+    assert torch.equal(O_host, O_dev.cpu())
+
+
+def test_host_buffer_api_rejects_device_tensors():
+    from blackflash_b200 import blackflash_host
+    q = torch.zeros(1, 1, 64, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="host"):
+        blackflash_host(q, q, q)

@@ -57,7 +57,12 @@ constexpr int kBN = 128;        // KV rows per tile
 constexpr int kQTiles = 2;      // query tiles per work item
 constexpr int kStages = 3;      // K/V ring depth
 constexpr int kSoftWarps = 16;                       // 8 per query tile, 4 per scheduler
-constexpr int kThreads = kSoftWarps * 32 + 3 * 32;   // + TMA producer, S issuer, PV issuer
+#ifndef BF_REGSPLIT
+#define BF_REGSPLIT 1
+#endif
+// With BF_REGSPLIT the block is 20 warps (a fourth, idle warp completes the last
+// warpgroup) so setmaxnreg can move registers from the issuer warps to the softmax.
+constexpr int kThreads = kSoftWarps * 32 + (BF_REGSPLIT ? 4 : 3) * 32;  // + TMA producer, S issuer, PV issuer
 constexpr int kTileBytes = kBM * kD * 2;  // 16 KiB (Q, K, V or O tile, bf16)
 constexpr int kTmemCols = 512;
 constexpr int kProducerWarp = 16;  // TMA producer
@@ -67,6 +72,13 @@ constexpr int kPVWarp = 18;        // issues O += P V
 constexpr bool kPerfDecouple = true;  // perf experiment only: MMA and softmax do not wait on each other
 #else
 constexpr bool kPerfDecouple = false;
+#endif
+#ifndef BF_LAZY_MAX
+#define BF_LAZY_MAX 0
+#endif
+constexpr bool kLazyMax = BF_LAZY_MAX != 0;
+#ifndef BF_DEFER_P
+#define BF_DEFER_P 0
 #endif
 #ifndef BF_EMU_PAIRS
 #define BF_EMU_PAIRS 2
@@ -215,6 +227,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = bars->tmem_base;
     const WaitCtl ctl{&bars->abort_flag, &g_wait_status, p.timeout_ns};
 
+#if BF_REGSPLIT
+    // Launch budget 96 x 640 = 61440: softmax 104 x 512 + issuers 64 x 128.
+    if (warp < kSoftWarps)
+        regs_inc<104>();
+    else
+        regs_dec<64>();
+#endif
     if (warp < kSoftWarps) {
         // ------------------------------------------------------------ softmax
         // Tile t has 8 warps. Warp w covers 16 TMEM lanes (rows) of its lane
@@ -242,6 +261,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* stage = smem + kOffO + t * kTileBytes;
         uint32_t g = 0;  // global KV step of this CTA
         bool ok = true;
+#if BF_DEFER_P
+        bool p_pending = false;  // P stored but p_full not yet signalled
+#endif
 
         for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
             int bh, q_row0;
@@ -260,9 +282,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t s[2][32];  // columns 64h + [0, 32) and 64h + [32, 64)
                 tmem_ld16x32bx2_x32<64>(tS + 0, s[0]);
                 tmem_ld16x32bx2_x32<64>(tS + 32, s[1]);
+#if BF_DEFER_P
+                if (p_pending) {
+                    // P of the previous step: its store latency overlaps this step's S load.
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(bar_p);
+                    p_pending = false;
+                }
+#endif
                 tmem_wait_ld();
-                tc_fence_before();
-                mbar_arrive(bar_se);  // S_t may now be overwritten by the next step's S_t
                 BF_TRACE(t, g, 2);
 
                 if (p.dbg_s != nullptr && item == 0 && t == 0 && j == 0) {
@@ -281,64 +310,110 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (c >= valid) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
                 }
 
-                float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < 32; c += 2) {
-                    mx0 = fmax3(mx0, __uint_as_float(s[0][c]), __uint_as_float(s[0][c + 1]));
-                    mx1 = fmax3(mx1, __uint_as_float(s[1][c]), __uint_as_float(s[1][c + 1]));
-                }
-                float mx = fmaxf(mx0, mx1);
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));  // the row's other half
-                m_raw = fmaxf(m_raw, mx);
-                const float m_new = mx * sl2;
-                BF_TRACE(t, g, 3);
-
-                // Lazy rescale: keep the old reference max unless the tile max exceeds
-                // it by more than 8 (log2 units), i.e. P entries stay <= 256.
-                const bool need = m_new > m_use + 8.0f;
-                float alpha = 1.f;
-                if (need) {
-                    alpha = fast_exp2(m_use - m_new);  // 0 on the first tile
-                    m_use = m_new;
-                }
-                l_half *= alpha;
-
-                const uint64_t negm_2 = f2_pack(-m_use, -m_use);
-                uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = f2_pack(0.f, 0.f);
+                // p = 2^(s * scale * log2 e - m): the argument is one packed FMA per pair;
+                // kEmuPairs of every 8 pairs take the FMA-pipe exp2, the rest MUFU ex2.
+                // Returns this thread's partial row sum; fills pk with bf16 pairs.
                 uint32_t pk[2][16];
+                auto exps = [&](float m_ref) -> float {
+                    const uint64_t negm_2 = f2_pack(-m_ref, -m_ref);
+                    uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = f2_pack(0.f, 0.f);
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
+                    for (int q = 0; q < 2; ++q) {
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        const uint64_t x2 = f2_fma(
-                            f2_pack(__uint_as_float(s[q][2 * c]), __uint_as_float(s[q][2 * c + 1])), sl2_2, negm_2);
-                        uint64_t p2;
+                        for (int c = 0; c < 16; ++c) {
+                            const uint64_t x2 = f2_fma(
+                                f2_pack(__uint_as_float(s[q][2 * c]), __uint_as_float(s[q][2 * c + 1])), sl2_2, negm_2);
+                            uint64_t p2;
 #ifdef BF_PERF_NO_EXP
-                        if (true) {
-                            p2 = x2;  // perf experiment only: exponentials skipped, results are wrong
-                        } else
+                            if (true) {
+                                p2 = x2;  // perf experiment only: exponentials skipped, results are wrong
+                            } else
 #endif
-                        if ((c & 7) < kEmuPairs) {
-                            p2 = exp2_poly_x2(x2);
-                        } else {
-                            float x0, x1;
-                            f2_unpack(x2, x0, x1);
-                            p2 = f2_pack(fast_exp2(x0), fast_exp2(x1));
+                            if ((c & 7) < kEmuPairs) {
+                                p2 = exp2_poly_x2<kLazyMax>(x2);
+                            } else {
+                                float x0, x1;
+                                f2_unpack(x2, x0, x1);
+                                p2 = f2_pack(fast_exp2(x0), fast_exp2(x1));
+                            }
+                            if (c & 1)
+                                sum_b = f2_add(sum_b, p2);
+                            else
+                                sum_a = f2_add(sum_a, p2);
+                            float p0, p1;
+                            f2_unpack(p2, p0, p1);
+                            pk[q][c] = pack_bf16x2(p0, p1);
                         }
-                        if (c & 1)
-                            sum_b = f2_add(sum_b, p2);
-                        else
-                            sum_a = f2_add(sum_a, p2);
-                        float p0, p1;
-                        f2_unpack(p2, p0, p1);
-                        pk[q][c] = pack_bf16x2(p0, p1);
                     }
-                }
-                {
                     float a0, a1, b0, b1;
                     f2_unpack(sum_a, a0, a1);
                     f2_unpack(sum_b, b0, b1);
-                    l_half += (a0 + a1) + (b0 + b1);
+                    return (a0 + a1) + (b0 + b1);
+                };
+                auto row_max = [&]() -> float {
+                    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+                    for (int c = 0; c < 32; c += 2) {
+                        mx0 = fmax3(mx0, __uint_as_float(s[0][c]), __uint_as_float(s[0][c + 1]));
+                        mx1 = fmax3(mx1, __uint_as_float(s[1][c]), __uint_as_float(s[1][c + 1]));
+                    }
+                    const float mx = fmaxf(mx0, mx1);
+                    return fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));  // the row's other half
+                };
+
+                bool need;
+                float alpha = 1.f;
+                if constexpr (!kLazyMax) {
+                    tc_fence_before();
+                    mbar_arrive(bar_se);  // S_t is in registers: it may now be overwritten
+                    const float mx = row_max();
+                    m_raw = fmaxf(m_raw, mx);
+                    const float m_new = mx * sl2;
+                    BF_TRACE(t, g, 3);
+                    // Lazy rescale: keep the old reference max unless the tile max exceeds
+                    // it by more than 8 (log2 units), i.e. P entries stay <= 256.
+                    need = m_new > m_use + 8.0f;
+                    if (need) {
+                        alpha = fast_exp2(m_use - m_new);  // 0 on the first tile
+                        m_use = m_new;
+                    }
+                    l_half = l_half * alpha + exps(m_use);
+                } else {
+                    // The tile max is computed only on a slice's first tile (or when row_max
+                    // is requested). Later tiles use the reference max directly and check the
+                    // row sum: it exceeds 2^16 (or is inf) exactly when some entry got large.
+                    // Then the max is taken from S (still in TMEM: s_empty is signalled only
+                    // after this check) and the tile is recomputed.
+                    if (j == 0 || p.row_max != nullptr) {
+                        const float mx = row_max();
+                        m_raw = fmaxf(m_raw, mx);
+                        if (j == 0) m_use = mx * sl2;
+                    }
+                    BF_TRACE(t, g, 3);
+                    float part = exps(m_use);
+                    const float tot = part + __shfl_xor_sync(0xffffffffu, part, 16);
+                    need = !(tot <= 65536.f);
+                    if (__any_sync(0xffffffffu, need)) {
+                        tmem_ld16x32bx2_x32<64>(tS + 0, s[0]);
+                        tmem_ld16x32bx2_x32<64>(tS + 32, s[1]);
+                        tmem_wait_ld();
+                        if (valid < 64) {
+#pragma unroll
+                            for (int c = 0; c < 64; ++c)
+                                if (c >= valid) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+                        }
+                        const float mx = row_max();
+                        m_raw = fmaxf(m_raw, mx);
+                        if (need) {
+                            const float m_new = mx * sl2;
+                            alpha = fast_exp2(m_use - m_new);
+                            m_use = m_new;
+                        }
+                        part = exps(m_use);
+                    }
+                    l_half = l_half * alpha + part;
+                    tc_fence_before();
+                    mbar_arrive(bar_se);  // no more reads of S_t
                 }
                 BF_TRACE(t, g, 4);
 
@@ -360,11 +435,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // bf16 P: this thread's 64 S columns are P columns 32h + [0, 32).
                 tmem_st16x32bx2_x16<32>(tP, pk[0]);
                 tmem_st16x32bx2_x16<32>(tP + 16, pk[1]);
+#if BF_DEFER_P
+                p_pending = true;  // completed and signalled early in the next step
+#else
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(bar_p);
+#endif
                 BF_TRACE(t, g, 6);
             }
+#if BF_DEFER_P
+            if (p_pending) {
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(bar_p);
+                p_pending = false;
+            }
+#endif
             if (!ok) break;
 
             // ---------------------------------------------------- epilogue of this item

@@ -323,15 +323,27 @@ def run_ours(args, cfg_name):
         dist_mod.destroy_process_group()
 
 
+SP_DESC = {
+    "allgather": "sp{world}: NCCL all-gather of K/V overlapping the own-block kernel, one gathered-block kernel, one LSE merge",
+    "ring": "ring{world}: NCCL send/recv per step, LSE merge per step",
+}
+# Our kernels per step: allgather = own block + gathered blocks + merge + cast (own block + cast
+# when alone); ring = world partials + (world - 1) merges + cast.
+SP_LAUNCHES = {"allgather": lambda w: 4 if w > 1 else 2, "ring": lambda w: 2 * w}
+
+
 def run_ring(args, cfg_name):
-    """Config 5: the sequence is split over the ranks; each step is one full ring pass
-    (world partial kernels, world-1 LSE merges, one bf16 cast per rank) with the next
-    KV block's NCCL send/recv overlapping the current block's kernel."""
+    """Config 5: the sequence is split over the ranks. Default schedule (--sp-mode
+    allgather): NCCL all-gather of K and V overlapping the own-block kernel, then one
+    kernel over the gathered blocks, one LSE merge and one bf16 cast per rank. The
+    P2P ring (--sp-mode ring) runs world partial kernels and world-1 merges with the
+    next KV block's send/recv overlapping the current block's kernel."""
     import torch.distributed as dist_mod
 
     from blackflash_b200.inputs import make_qkv
-    from blackflash_b200.ring import ring_attention
+    from blackflash_b200.ring import allgather_attention, ring_attention
 
+    sp = allgather_attention if args.sp_mode == "allgather" else ring_attention
     world, rank, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
@@ -348,7 +360,7 @@ def run_ring(args, cfg_name):
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        return ring_attention(q, k, v, scale)
+        return sp(q, k, v, scale)
 
     def barrier():
         if world > 1:
@@ -387,7 +399,7 @@ def run_ring(args, cfg_name):
     oh = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
 
     def e2e_step():
-        o = ring_attention(qh.to(dev, non_blocking=True), kh.to(dev, non_blocking=True),
+        o = sp(qh.to(dev, non_blocking=True), kh.to(dev, non_blocking=True),
                            vh.to(dev, non_blocking=True), scale)
         oh.copy_(o, non_blocking=True)
 
@@ -416,8 +428,8 @@ def run_ring(args, cfg_name):
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal, sequence-parallel ring",
-                       "global_batch": B, "seq_len": N, "parallelism": f"ring{world} (NCCL send/recv, LSE merge)",
+            "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal, sequence-parallel",
+                       "global_batch": B, "seq_len": N, "parallelism": SP_DESC[args.sp_mode].format(world=world),
                        "l2": "inputs larger than L2 (no flush)"},
             "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": per_gpu / peaks["bf16_tflops"], "traffic": None,
@@ -428,7 +440,7 @@ def run_ring(args, cfg_name):
             "e2e": {"value": f_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
                     "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": q.numel() * 2,
                     "ms_per_step": e2e_ms},
-            "gpu_launches": args.steps * (2 * world),
+            "gpu_launches": args.steps * (SP_LAUNCHES[args.sp_mode](world)),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -446,6 +458,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sp-mode", choices=["allgather", "ring"], default="allgather",
+                    help="sequence-parallel schedule of config 5")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -18,6 +18,7 @@ EXPORTED = (
     "blackflash_fwd",
     "blackflash_fwd_causal",
     "blackflash_fwd_partial",
+    "blackflash_fwd_partial_blocks",
     "blackflash_lse_merge",
     "blackflash_f32_to_bf16",
     "blackflash_status",
@@ -37,6 +38,7 @@ _SIGS = {
     "blackflash_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp]),
     "blackflash_fwd_causal": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp]),
     "blackflash_fwd_partial": (_i, [_vp, _vp, _vp, _vp, _vp, _ll, _i, _i, _i, _f, _vp]),
+    "blackflash_fwd_partial_blocks": (_i, [_vp, _vp, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _f, _vp]),
     "blackflash_lse_merge": (_i, [_vp, _vp, _vp, _vp, _ll, _i, _vp]),
     "blackflash_f32_to_bf16": (_i, [_vp, _vp, _ll, _vp]),
     "blackflash_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),

@@ -84,6 +84,35 @@ extern "C" int blackflash_fwd_partial(const void* Q, const void* K, const void* 
     return bf_fwd_launch(&a);
 }
 
+extern "C" int blackflash_fwd_partial_blocks(const void* Q, const void* Kg, const void* Vg, float* O_f32, float* lse,
+                                             long long BH, int Nq, int n_blocks, int block_rows, int skip, int d,
+                                             float scale, void* stream) {
+    g_last_error[0] = 0;
+    if (!O_f32 || !lse) return bf_set_error(BF_ERR_ARG, "partial mode needs O_f32 and lse");
+    if (block_rows % 128) return bf_set_error(BF_ERR_ARG, "block_rows must be a multiple of 128");
+    if (n_blocks < 1 || block_rows <= 0 || skip < -1 || skip >= n_blocks || (skip >= 0 && n_blocks == 1))
+        return bf_set_error(BF_ERR_ARG, "need n_blocks >= 1, block_rows >= 1, -1 <= skip < n_blocks, a block left");
+    const long long n_kv = (long long)(n_blocks - (skip >= 0)) * block_rows;
+    if (n_kv > 0x7fffffffLL) return bf_set_error(BF_ERR_ARG, "too many KV rows");
+    BfFwdArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = Q;
+    a.k = Kg;
+    a.v = Vg;
+    a.o_f32 = O_f32;
+    a.lse = lse;
+    a.bh = BH;
+    a.n_q = Nq;
+    a.n_kv = (int)n_kv;
+    a.d = d;
+    a.scale = scale;
+    a.stream = stream;
+    a.kv_blocks = n_blocks;
+    a.kv_block_rows = block_rows;
+    a.kv_skip = skip;
+    return bf_fwd_launch(&a);
+}
+
 extern "C" int blackflash_fwd_timeout_probe(const void* Q, const void* K, const void* V, void* O, int B, int H, int N,
                                             int d, float scale, unsigned long long timeout_ns, void* stream) {
     g_last_error[0] = 0;

@@ -140,7 +140,25 @@ struct KParams {
     int causal;        // key j visible to query i only if j <= i (top-left aligned)
     long long* trace;  // kTrace builds: clock64 event stamps of CTA `trace_cta`
     int trace_cta;
+    // Blocked KV: K/V maps cover [kv_blocks * bh] slices of kv_blk_tiles * 128 rows; KV tile j
+    // of slice bh lives in block j / kv_blk_tiles (past kv_skip) at slice block * bh_count + bh.
+    int kv_blk_tiles;  // 0: plain layout
+    int kv_skip;       // block left out, -1 for none
+    int bh_count;
 };
+
+// KV tile j of slice bh -> (row, slice) coordinates in the K/V tensor maps.
+__device__ __forceinline__ void kv_coords(const KParams& p, int j, int bh, int& row, int& slice) {
+    if (p.kv_blk_tiles == 0) {
+        row = j * kBN;
+        slice = bh;
+        return;
+    }
+    int blk = j / p.kv_blk_tiles;
+    if (p.kv_skip >= 0 && blk >= p.kv_skip) ++blk;
+    row = (j - (j / p.kv_blk_tiles) * p.kv_blk_tiles) * kBN;
+    slice = blk * p.bh_count + bh;
+}
 
 // Pipeline event trace (diagnostic builds only): trace[role * 512 + g * 8 + ev]
 // holds clock64() - t0 of CTA p.trace_cta for its first 64 global KV steps.
@@ -535,11 +553,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             last_q = it;
             __syncwarp();
             for (int j = 0; j < nk_item; ++j, ++c) {
+                int kv_row, kv_slice;
+                kv_coords(p, j, bh, kv_row, kv_slice);
                 if (!(ok = warp_wait(k_empty0 + 8 * st, par, ctl, kSiteProdKEmpty))) break;
                 if (!p.skip_k_loads) {
                     if (leader) {
                         mbar_arrive_expect_tx(k_full0 + 8 * st, kTileBytes);
-                        tma_load_3d(k_smem0 + st * kTileBytes, &tmK, k_full0 + 8 * st, 0, j * kBN, bh);
+                        tma_load_3d(k_smem0 + st * kTileBytes, &tmK, k_full0 + 8 * st, 0, kv_row, kv_slice);
                     }
                     BF_TRACE(3, c, 0);
                     last_k = (int)c;
@@ -547,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!(ok = warp_wait(v_empty0 + 8 * st, par, ctl, kSiteProdVEmpty))) break;
                 if (leader) {
                     mbar_arrive_expect_tx(v_full0 + 8 * st, kTileBytes);
-                    tma_load_3d(v_smem0 + st * kTileBytes, &tmV, v_full0 + 8 * st, 0, j * kBN, bh);
+                    tma_load_3d(v_smem0 + st * kTileBytes, &tmV, v_full0 + 8 * st, 0, kv_row, kv_slice);
                 }
                 BF_TRACE(3, c, 1);
                 last_v = (int)c;
@@ -770,8 +790,21 @@ int bf_fwd_launch(const BfFwdArgs* a) {
     CUtensorMap mq, mk, mv, mo;
     int rc;
     if ((rc = make_map(&mq, a->q, a->bh, a->n_q)) != BF_OK) return rc;
-    if ((rc = make_map(&mk, a->k, a->bh, a->n_kv)) != BF_OK) return rc;
-    if ((rc = make_map(&mv, a->v, a->bh, a->n_kv)) != BF_OK) return rc;
+    int kv_blk_tiles = 0;
+    if (a->kv_blocks) {
+        if (a->kv_blocks < 1 || a->kv_block_rows <= 0 || a->kv_block_rows % bfk::kBN ||
+            a->kv_skip < -1 || a->kv_skip >= a->kv_blocks || a->causal)
+            return bf_set_error(BF_ERR_ARG, "blocked KV needs block rows % 128 == 0, -1 <= skip < blocks, non-causal");
+        if (a->n_kv != (a->kv_blocks - (a->kv_skip >= 0)) * (long long)a->kv_block_rows)
+            return bf_set_error(BF_ERR_ARG, "blocked KV: n_kv must equal the rows of the blocks used");
+        if ((long long)a->kv_blocks * a->bh > 0x7fffffffLL) return bf_set_error(BF_ERR_ARG, "problem too large for one launch");
+        kv_blk_tiles = a->kv_block_rows / bfk::kBN;
+        if ((rc = make_map(&mk, a->k, (long long)a->kv_blocks * a->bh, a->kv_block_rows)) != BF_OK) return rc;
+        if ((rc = make_map(&mv, a->v, (long long)a->kv_blocks * a->bh, a->kv_block_rows)) != BF_OK) return rc;
+    } else {
+        if ((rc = make_map(&mk, a->k, a->bh, a->n_kv)) != BF_OK) return rc;
+        if ((rc = make_map(&mv, a->v, a->bh, a->n_kv)) != BF_OK) return rc;
+    }
     if (a->o) {
         if ((rc = make_map(&mo, a->o, a->bh, a->n_q)) != BF_OK) return rc;
     } else {
@@ -794,6 +827,9 @@ int bf_fwd_launch(const BfFwdArgs* a) {
     kp.trace = a->trace;
     kp.causal = a->causal;
     kp.trace_cta = a->trace_cta;
+    kp.kv_blk_tiles = kv_blk_tiles;
+    kp.kv_skip = a->kv_blocks ? a->kv_skip : -1;
+    kp.bh_count = (int)a->bh;
 
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(a->stream);
     if (a->trace) {

@@ -24,6 +24,12 @@ struct BfFwdArgs {
     long long* trace;
     int trace_cta;
     int causal;  // 1: key j visible to query i only if j <= i
+    // Blocked KV (sequence-parallel gather): K and V are [kv_blocks, bh, kv_block_rows, 64]
+    // and the slice's keys are the concatenation of every block except kv_skip (-1: none).
+    // kv_blocks == 0 means the plain [bh, n_kv, 64] layout.
+    int kv_blocks;
+    int kv_block_rows;
+    int kv_skip;
 };
 
 int bf_fwd_launch(const BfFwdArgs* a);

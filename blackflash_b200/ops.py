@@ -108,6 +108,27 @@ def attention_partial(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: 
     return O, lse
 
 
+def attention_partial_blocks(Q: torch.Tensor, Kg: torch.Tensor, Vg: torch.Tensor, scale: float, skip: int = -1):
+    """Q [S, Nq, 64] against the gathered blocks Kg, Vg [G, S, n, 64] with block `skip`
+    left out (-1: all blocks). n must be a multiple of 128.
+
+    Returns (O_f32 [S, Nq, 64], lse [S, Nq]) over the concatenated used blocks."""
+    for name, t in (("Q", Q), ("Kg", Kg), ("Vg", Vg)):
+        _require(t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous(), f"{name} must be a contiguous CUDA bf16 tensor")
+    _require(Q.dim() == 3 and Kg.dim() == 4 and Kg.shape == Vg.shape and Q.size(2) == 64 and Kg.size(3) == 64
+             and Kg.size(1) == Q.size(0), "partial_blocks needs Q [S,Nq,64] and Kg, Vg [G,S,n,64]")
+    S, Nq, _ = Q.shape
+    G, _, n, _ = Kg.shape
+    O = torch.empty((S, Nq, 64), dtype=torch.float32, device=Q.device)
+    lse = torch.empty((S, Nq), dtype=torch.float32, device=Q.device)
+    lib = _lib.load()
+    with torch.cuda.device(Q.device):
+        rc = lib.blackflash_fwd_partial_blocks(Q.data_ptr(), Kg.data_ptr(), Vg.data_ptr(), O.data_ptr(), lse.data_ptr(),
+                                               S, Nq, G, n, int(skip), 64, float(scale), _stream_handle(Q.device))
+    _lib.check(rc, "blackflash_fwd_partial_blocks")
+    return O, lse
+
+
 def lse_merge_(O_acc: torch.Tensor, lse_acc: torch.Tensor, O_part: torch.Tensor, lse_part: torch.Tensor) -> None:
     """In-place log-sum-exp merge of a partial result into the running one (fp32)."""
     for t in (O_acc, lse_acc, O_part, lse_part):

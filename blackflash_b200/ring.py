@@ -16,7 +16,14 @@ rank attends its Q block to every KV block:
 The received block lands in a local HBM buffer before any kernel reads it, so no
 kernel reads peer memory and no TMA multicast is involved.
 
-The schedule is independent of the compute: `partial_fn`, `merge_fn` and
+`allgather_attention` is the faster schedule for one NVSwitch node: an NCCL
+all-gather of K and V into a local [G, S, n, 64] buffer runs while this rank's
+own block is computed; then one kernel covers the other G-1 blocks straight
+out of the gathered buffer (its producer maps KV tile -> block), and a single
+LSE merge combines the two partials. Each KV block crosses NVLink once per rank
+in one collective rather than G-1 dependent P2P steps, and G-2 merges go away.
+
+The schedules are independent of the compute: `partial_fn`, `merge_fn` and
 `finalize_fn` default to the sm_100a kernels, and the CPU tests substitute
 torch restatements to run the same schedule on gloo ranks.
 """
@@ -80,5 +87,48 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
             r.wait()
         if step < world - 1:
             cur_k, cur_v = spare[step % 2]
+    out = finalize_fn(o_acc)
+    return (out, lse_acc) if return_lse else out
+
+
+def _default_partial_blocks(q, kg, vg, scale, skip):
+    from .ops import attention_partial_blocks
+    return attention_partial_blocks(q, kg, vg, scale, skip)
+
+
+def allgather_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, group=None,
+                        partial_fn: Callable = _default_partial, partial_blocks_fn: Callable = _default_partial_blocks,
+                        merge_fn: Callable = _default_merge, finalize_fn: Callable = _default_finalize,
+                        return_lse: bool = False):
+    """Same result as `ring_attention`, scheduled as all-gather + two partial kernels.
+
+    q, k, v: [S, n, 64] bf16, this rank's sequence block; n a multiple of 128 when
+    world > 1 (the gathered-block kernel's tiles never straddle two blocks).
+    """
+    if dist.is_available() and dist.is_initialized():
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+    else:
+        world, rank = 1, 0
+    if k.shape != v.shape or q.shape[0] != k.shape[0]:
+        raise RuntimeError("allgather_attention: q [S,n,64] and k, v [S,m,64] with equal S required")
+    if world == 1:
+        o, lse = partial_fn(q, k, v, scale)
+        out = finalize_fn(o)
+        return (out, lse) if return_lse else out
+    if k.shape[1] % 128:
+        raise RuntimeError("allgather_attention: the per-rank KV block must have a multiple of 128 rows")
+    kg = torch.empty((world,) + tuple(k.shape), dtype=k.dtype, device=k.device)
+    vg = torch.empty_like(kg)
+    if dist.get_backend(group) == "nccl":
+        works = [dist.all_gather_into_tensor(kg, k.contiguous(), group=group, async_op=True),
+                 dist.all_gather_into_tensor(vg, v.contiguous(), group=group, async_op=True)]
+    else:
+        works = [dist.all_gather(list(kg.unbind(0)), k.contiguous(), group=group, async_op=True),
+                 dist.all_gather(list(vg.unbind(0)), v.contiguous(), group=group, async_op=True)]
+    o_acc, lse_acc = partial_fn(q, k, v, scale)  # own block, overlapping the gather
+    for w in works:
+        w.wait()
+    o_rem, lse_rem = partial_blocks_fn(q, kg, vg, scale, rank)
+    merge_fn(o_acc, lse_acc, o_rem, lse_rem)
     out = finalize_fn(o_acc)
     return (out, lse_acc) if return_lse else out

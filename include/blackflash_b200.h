@@ -63,6 +63,20 @@ int blackflash_fwd_partial(const void* Q, const void* K, const void* V, float* O
                            int Nq, int Nkv, int d, float scale, void* stream);
 
 /*
+ * Partial attention of one query block against gathered KV blocks: the
+ * sequence-parallel mode's second kernel, after an all-gather of K and V.
+ * No counterpart in the reference.
+ *   Q:      [BH, Nq, 64] bf16
+ *   Kg, Vg: [n_blocks, BH, block_rows, 64] bf16 (rank-major, as an all-gather lays it out)
+ *   skip:   block left out (the caller's own, already computed), or -1 to use all
+ *   O_f32, lse as in blackflash_fwd_partial, over the concatenation of the used
+ *   blocks. block_rows must be a multiple of 128.
+ */
+int blackflash_fwd_partial_blocks(const void* Q, const void* Kg, const void* Vg, float* O_f32, float* lse,
+                                  long long BH, int Nq, int n_blocks, int block_rows, int skip, int d, float scale,
+                                  void* stream);
+
+/*
  * Log-sum-exp merge of one partial result into a running one, in place:
  *   lse' = log(exp(lse_acc) + exp(lse_part))
  *   O'   = O_acc * exp(lse_acc - lse') + O_part * exp(lse_part - lse')

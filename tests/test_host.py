@@ -57,6 +57,9 @@ def test_argument_errors_without_device_work():
     assert rc == _lib.BF_ERR_ARG
     rc = lib.blackflash_fwd_partial(16, 16, 16, None, None, 1, 64, 64, 64, 0.125, None)
     assert rc == _lib.BF_ERR_ARG
+    for blocks, rows, skip in ((0, 128, -1), (2, 100, 0), (2, 128, 2), (1, 128, 0), (2, 128, -2)):
+        rc = lib.blackflash_fwd_partial_blocks(16, 16, 16, 16, 16, 1, 64, blocks, rows, skip, 64, 0.125, None)
+        assert rc == _lib.BF_ERR_ARG, (blocks, rows, skip)
     rc = lib.blackflash_lse_merge(16, 16, 16, 16, 4, 32, None)
     assert rc == _lib.BF_ERR_ARG
     assert lib.blackflash_lse_merge(16, 16, 16, 16, 0, 64, None) == _lib.BF_OK
@@ -108,14 +111,25 @@ def _cpu_merge(o_acc, lse_acc, o_p, lse_p):
     lse_acc.copy_(m + torch.log(tot))
 
 
-def _ring_worker(rank, world, port, q, k, v, out_path):
+def _cpu_partial_blocks(q, kg, vg, scale, skip):
+    """The gathered-block kernel's contract: keys are the used blocks, concatenated."""
+    used = [g for g in range(kg.shape[0]) if g != skip]
+    return _cpu_partial(q, torch.cat([kg[g] for g in used], dim=1), torch.cat([vg[g] for g in used], dim=1), scale)
+
+
+def _ring_worker(rank, world, port, q, k, v, out_path, mode="ring"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    from blackflash_b200.ring import ring_attention
+    from blackflash_b200.ring import allgather_attention, ring_attention
     n = q.shape[1] // world
     sl = slice(rank * n, (rank + 1) * n)
-    o, lse = ring_attention(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125,
-                            partial_fn=_cpu_partial, merge_fn=_cpu_merge, finalize_fn=lambda x: x, return_lse=True)
+    args = (q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125)
+    if mode == "ring":
+        o, lse = ring_attention(*args, partial_fn=_cpu_partial, merge_fn=_cpu_merge, finalize_fn=lambda x: x,
+                                return_lse=True)
+    else:
+        o, lse = allgather_attention(*args, partial_fn=_cpu_partial, partial_blocks_fn=_cpu_partial_blocks,
+                                     merge_fn=_cpu_merge, finalize_fn=lambda x: x, return_lse=True)
     torch.save({"o": o, "lse": lse}, f"{out_path}.{rank}")
     dist.barrier()
     dist.destroy_process_group()
@@ -135,6 +149,22 @@ def test_ring_schedule_on_gloo_matches_full_attention(world, tmp_path):
     q, k, v = (t.reshape(2, 96 * world, 64) for t in (q, k, v))
     out = str(tmp_path / "ring")
     mp.spawn(_ring_worker, args=(world, _free_port(), q, k, v, out), nprocs=world, join=True)
+    o = torch.cat([torch.load(f"{out}.{r}")["o"] for r in range(world)], dim=1).numpy()
+    lse = torch.cat([torch.load(f"{out}.{r}")["lse"] for r in range(world)], dim=1).numpy()
+    o_ref, lse_ref, _ = oracle.attn_exact(q, k, v, 0.125)
+    np.testing.assert_allclose(o, o_ref, atol=2e-5)
+    np.testing.assert_allclose(lse, lse_ref, atol=2e-4)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_allgather_schedule_on_gloo_matches_full_attention(world, tmp_path):
+    from blackflash_b200.inputs import make_qkv
+    from oracle import oracle
+    n = 128 * world
+    q, k, v = make_qkv(1, 2, n, dist="peaked", seed=10 + world)
+    q, k, v = (t.reshape(2, n, 64) for t in (q, k, v))
+    out = str(tmp_path / "ag")
+    mp.spawn(_ring_worker, args=(world, _free_port(), q, k, v, out, "allgather"), nprocs=world, join=True)
     o = torch.cat([torch.load(f"{out}.{r}")["o"] for r in range(world)], dim=1).numpy()
     lse = torch.cat([torch.load(f"{out}.{r}")["lse"] for r in range(world)], dim=1).numpy()
     o_ref, lse_ref, _ = oracle.attn_exact(q, k, v, 0.125)

@@ -57,35 +57,65 @@ def test_partial_ragged_blocks():
     np.testing.assert_allclose(lse.cpu().numpy(), lse_ref, atol=2e-3)
 
 
+@pytest.mark.parametrize("skip", [-1, 0, 2, 3])
+def test_partial_blocks_matches_oracle(skip):
+    """Gathered-block kernel: keys are blocks [G, S, n, 64] minus `skip`, concatenated."""
+    from blackflash_b200 import attention_partial_blocks
+    from blackflash_b200.inputs import make_qkv
+    S, nq, n, G = 3, 300, 256, 4
+    q, _, _ = make_qkv(1, S, nq, seed=41, device="cuda")
+    _, kg, vg = make_qkv(G, S, n, dist="peaked", seed=42, device="cuda")  # [G, S, n, 64]
+    q3 = q.reshape(S, nq, 64)
+    o, lse = attention_partial_blocks(q3, kg, vg, 0.125, skip)
+    torch.cuda.synchronize()
+    used = [g for g in range(G) if g != skip]
+    k_cat = torch.cat([kg[g] for g in used], dim=1).cpu()
+    v_cat = torch.cat([vg[g] for g in used], dim=1).cpu()
+    o_ref, lse_ref, _ = oracle.attn_exact(q3.cpu(), k_cat, v_cat, 0.125)
+    d = np.abs(o.cpu().numpy() - o_ref)
+    assert d.max() <= 1e-2 and d.mean() <= 1e-3
+    np.testing.assert_allclose(lse.cpu().numpy(), lse_ref, atol=2e-3)
+
+
+def test_partial_blocks_rejects_unaligned_blocks():
+    from blackflash_b200 import attention_partial_blocks
+    q = torch.zeros(2, 128, 64, device="cuda", dtype=torch.bfloat16)
+    kg = torch.zeros(2, 2, 192, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="multiple of 128"):
+        attention_partial_blocks(q, kg, kg, 0.125, 0)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _ring_worker(rank, world, port, qkv, out):
+def _ring_worker(rank, world, port, qkv, out, mode="ring"):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
-    from blackflash_b200.ring import ring_attention
+    from blackflash_b200.ring import allgather_attention, ring_attention
     q, k, v = (t.cuda() for t in qkv)
     n = q.shape[1] // world
     sl = slice(rank * n, (rank + 1) * n)
-    o = ring_attention(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125)
+    fn = ring_attention if mode == "ring" else allgather_attention
+    o = fn(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125)
     torch.save(o.cpu(), f"{out}.{rank}")
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
-def test_ring_over_nccl(tmp_path):
+@pytest.mark.parametrize("mode", ["ring", "allgather"])
+def test_ring_over_nccl(tmp_path, mode):
     from blackflash_b200.inputs import make_qkv
     world = min(torch.cuda.device_count(), 4)
     S, N = 4, 512 * world
     q, k, v = (t.reshape(S, N, 64) for t in make_qkv(1, S, N, seed=77))
     out = str(tmp_path / "ring")
-    mp.spawn(_ring_worker, args=(world, _free_port(), (q, k, v), out), nprocs=world, join=True)
+    mp.spawn(_ring_worker, args=(world, _free_port(), (q, k, v), out, mode), nprocs=world, join=True)
     o = torch.cat([torch.load(f"{out}.{r}") for r in range(world)], dim=1).float().numpy()
     o_ref, _, _ = oracle.attn_exact(q, k, v, 0.125)
     d = np.abs(o - o_ref)

@@ -51,10 +51,10 @@ CONFIGS = {
 METRIC = "attention fwd TFLOPS (4BHN^2d/t)"
 
 # DRAM bytes (read + write) per launch of the main kernel for config 3 at N=1. Measured by
-# ncu on a quarter-size case (profiles/fa_fwd_sm100_b16h64n1024.md: 402.8 MB read +
-# 112.6 MB written for 1024 slices) and scaled by 4; traffic is linear in the slice count
+# ncu on a quarter-size case (profiles/fa_fwd_sm100_b16h64n1024.md: 402.7 MB read +
+# 114.5 MB written for 1024 slices) and scaled by 4; traffic is linear in the slice count
 # because every slice is independent.
-TRAFFIC_BYTES = {"3": 4 * (402.789888e6 + 112.627456e6)}
+TRAFFIC_BYTES = {"3": 4 * (402.700032e6 + 114.543360e6)}
 
 
 def flops(B, H, N, d):

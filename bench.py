@@ -324,26 +324,36 @@ def run_ours(args, cfg_name):
 
 
 SP_DESC = {
+    "ring": "ring{world}: KV rotated both ways round the ring by NCCL send/recv, two blocks per step in one kernel, LSE merge per step",
+    "ring1": "ring{world}: KV rotated one way by NCCL send/recv, one block per step, LSE merge per step",
     "allgather": "sp{world}: NCCL all-gather of K/V overlapping the own-block kernel, one gathered-block kernel, one LSE merge",
-    "ring": "ring{world}: NCCL send/recv per step, LSE merge per step",
 }
-# Our kernels per step: allgather = own block + gathered blocks + merge + cast (own block + cast
-# when alone); ring = world partials + (world - 1) merges + cast.
-SP_LAUNCHES = {"allgather": lambda w: 4 if w > 1 else 2, "ring": lambda w: 2 * w}
+
+
+def sp_launches(mode: str, w: int) -> int:
+    """Our kernels per step (partials, merges, the bf16 cast)."""
+    if mode == "allgather":
+        return 4 if w > 1 else 2
+    if mode == "ring" and w > 2:
+        return 1 + 2 * (w // 2) + 1
+    return 2 * w
 
 
 def run_ring(args, cfg_name):
-    """Config 5: the sequence is split over the ranks. Default schedule (--sp-mode
-    allgather): NCCL all-gather of K and V overlapping the own-block kernel, then one
-    kernel over the gathered blocks, one LSE merge and one bf16 cast per rank. The
-    P2P ring (--sp-mode ring) runs world partial kernels and world-1 merges with the
-    next KV block's send/recv overlapping the current block's kernel."""
+    """Config 5: the sequence is split over the ranks and KV rotates round the ring
+    (NCCL send/recv into local buffers, overlapping the kernels; LSE merge per step).
+    --sp-mode ring (default) rotates both ways, two blocks per step in one launch;
+    ring1 is the one-way ring; allgather replaces the rotation by one all-gather."""
     import torch.distributed as dist_mod
 
     from blackflash_b200.inputs import make_qkv
     from blackflash_b200.ring import allgather_attention, ring_attention
 
-    sp = allgather_attention if args.sp_mode == "allgather" else ring_attention
+    if args.sp_mode == "allgather":
+        sp = allgather_attention
+    else:
+        def sp(q_, k_, v_, scale_):
+            return ring_attention(q_, k_, v_, scale_, bidirectional=(args.sp_mode == "ring"))
     world, rank, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
@@ -440,7 +450,7 @@ def run_ring(args, cfg_name):
             "e2e": {"value": f_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
                     "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": q.numel() * 2,
                     "ms_per_step": e2e_ms},
-            "gpu_launches": args.steps * (SP_LAUNCHES[args.sp_mode](world)),
+            "gpu_launches": args.steps * sp_launches(args.sp_mode, world),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -458,7 +468,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--sp-mode", choices=["allgather", "ring"], default="allgather",
+    ap.add_argument("--sp-mode", choices=["ring", "ring1", "allgather"], default="ring",
                     help="sequence-parallel schedule of config 5")
     args = ap.parse_args()
     if args.warmup < 3:

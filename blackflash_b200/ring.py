@@ -13,6 +13,12 @@ rank attends its Q block to every KV block:
             next one from rank r-1 (torch.distributed P2P; NCCL over NVLink on
             GPUs), so the transfer overlaps the step's kernel.
 
+By default the rotation runs both ways round the ring (`bidirectional=True`):
+rank r receives blocks r-1, r-2, ... from the left and r+1, r+2, ... from the
+right, two per step, and computes each pair in one gathered-block launch. The
+classic one-way ring stays available (and is used for 2 ranks or per-rank blocks
+that are not a multiple of 128 rows).
+
 The received block lands in a local HBM buffer before any kernel reads it, so no
 kernel reads peer memory and no TMA multicast is involved.
 
@@ -52,11 +58,22 @@ def _default_finalize(o_acc):
 
 def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, group=None,
                    partial_fn: Callable = _default_partial, merge_fn: Callable = _default_merge,
-                   finalize_fn: Callable = _default_finalize, return_lse: bool = False):
+                   finalize_fn: Callable = _default_finalize, return_lse: bool = False,
+                   bidirectional: bool = True, partial_blocks_fn: Callable | None = None):
     """This rank's rows of softmax(scale Q K^T) V over the full (all-rank) sequence.
 
     q, k, v: [S, n_local, 64] bf16 (S = B*H slices), this rank's sequence block.
     Returns bf16 O [S, n_local, 64] (and the fp32 lse [S, n_local] if return_lse).
+
+    bidirectional=True (default) rotates KV both ways round the ring: at step s
+    this rank holds the blocks of ranks r-s (arrived from the left) and r+s (from
+    the right), computes both in one gathered-block launch, and forwards each one
+    further in its direction. Two neighbours are in flight at once, and the
+    G-1 foreign blocks arrive in floor(G/2) steps instead of G-1. NCCL's P2P
+    bandwidth per peer pair falls as the rank count grows (measured on 8 B200s:
+    81 GB/s per direction for one neighbour, 251 GB/s at 2 ranks), so a
+    one-directional ring is transfer-bound there. bidirectional=False is the
+    classic ring: one block per step, from the left.
     """
     if dist.is_available() and dist.is_initialized():
         world, rank = dist.get_world_size(group), dist.get_rank(group)
@@ -64,6 +81,9 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
         world, rank = 1, 0  # one process: the ring degenerates to a single partial step
     if k.shape != v.shape or q.shape[0] != k.shape[0]:
         raise RuntimeError("ring_attention: q [S,n,64] and k, v [S,m,64] with equal S required")
+    if world > 2 and bidirectional and k.shape[1] % 128 == 0:
+        return _ring_bidirectional(q, k, v, scale, group, world, rank, partial_fn,
+                                   partial_blocks_fn or _default_partial_blocks, merge_fn, finalize_fn, return_lse)
     nxt = dist.get_global_rank(group, (rank + 1) % world) if group is not None else (rank + 1) % world
     prv = dist.get_global_rank(group, (rank - 1) % world) if group is not None else (rank - 1) % world
 
@@ -87,6 +107,48 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
             r.wait()
         if step < world - 1:
             cur_k, cur_v = spare[step % 2]
+    out = finalize_fn(o_acc)
+    return (out, lse_acc) if return_lse else out
+
+
+def _ring_bidirectional(q, k, v, scale, group, world, rank, partial_fn, partial_blocks_fn, merge_fn, finalize_fn,
+                        return_lse):
+    """Both-way KV rotation (world >= 3). Blocks r-1 .. r-nl come from the left,
+    r+1 .. r+nr from the right, nl = floor(G/2), nr = ceil(G/2) - 1, so every
+    foreign block arrives exactly once. Step s >= 1 holds L_s (block r-s) in slot
+    0 and R_s (block r+s, s <= nr) in slot 1 of a [2, S, n, 64] pair buffer."""
+    g = (lambda x: dist.get_global_rank(group, x % world)) if group is not None else (lambda x: x % world)
+    right, left = g(rank + 1), g(rank - 1)
+    nl, nr = world // 2, (world + 1) // 2 - 1
+    pair_k = [torch.empty((2,) + tuple(k.shape), dtype=k.dtype, device=k.device) for _ in range(2)]
+    pair_v = [torch.empty_like(pair_k[0]) for _ in range(2)]
+
+    def exchange(step, src_l, src_r):
+        """Post the transfers that fill step+1's pair buffer."""
+        dst_k, dst_v = pair_k[(step + 1) % 2], pair_v[(step + 1) % 2]
+        ops = []
+        if step + 1 <= nl:  # L_{s+1} = block r-s-1: the left neighbour forwards its L_s
+            ops += [dist.P2POp(dist.isend, src_l[0], right, group), dist.P2POp(dist.isend, src_l[1], right, group),
+                    dist.P2POp(dist.irecv, dst_k[0], left, group), dist.P2POp(dist.irecv, dst_v[0], left, group)]
+        if step + 1 <= nr:  # R_{s+1} = block r+s+1: the right neighbour forwards its R_s
+            ops += [dist.P2POp(dist.isend, src_r[0], left, group), dist.P2POp(dist.isend, src_r[1], left, group),
+                    dist.P2POp(dist.irecv, dst_k[1], right, group), dist.P2POp(dist.irecv, dst_v[1], right, group)]
+        return dist.batch_isend_irecv(ops) if ops else []
+
+    reqs = exchange(0, (k, v), (k, v))
+    o_acc, lse_acc = partial_fn(q, k, v, scale)
+    for r in reqs:
+        r.wait()
+    for step in range(1, nl + 1):
+        ck, cv = pair_k[step % 2], pair_v[step % 2]
+        reqs = exchange(step, (ck[0], cv[0]), (ck[1], cv[1]))
+        if step <= nr:
+            o_p, lse_p = partial_blocks_fn(q, ck, cv, scale, -1)  # L_s and R_s in one launch
+        else:
+            o_p, lse_p = partial_fn(q, ck[0], cv[0], scale)
+        merge_fn(o_acc, lse_acc, o_p, lse_p)
+        for r in reqs:
+            r.wait()
     out = finalize_fn(o_acc)
     return (out, lse_acc) if return_lse else out
 

@@ -124,9 +124,9 @@ def _ring_worker(rank, world, port, q, k, v, out_path, mode="ring"):
     n = q.shape[1] // world
     sl = slice(rank * n, (rank + 1) * n)
     args = (q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125)
-    if mode == "ring":
+    if mode in ("ring", "ring2"):
         o, lse = ring_attention(*args, partial_fn=_cpu_partial, merge_fn=_cpu_merge, finalize_fn=lambda x: x,
-                                return_lse=True)
+                                return_lse=True, bidirectional=(mode == "ring2"), partial_blocks_fn=_cpu_partial_blocks)
     else:
         o, lse = allgather_attention(*args, partial_fn=_cpu_partial, partial_blocks_fn=_cpu_partial_blocks,
                                      merge_fn=_cpu_merge, finalize_fn=lambda x: x, return_lse=True)
@@ -149,6 +149,23 @@ def test_ring_schedule_on_gloo_matches_full_attention(world, tmp_path):
     q, k, v = (t.reshape(2, 96 * world, 64) for t in (q, k, v))
     out = str(tmp_path / "ring")
     mp.spawn(_ring_worker, args=(world, _free_port(), q, k, v, out), nprocs=world, join=True)
+    o = torch.cat([torch.load(f"{out}.{r}")["o"] for r in range(world)], dim=1).numpy()
+    lse = torch.cat([torch.load(f"{out}.{r}")["lse"] for r in range(world)], dim=1).numpy()
+    o_ref, lse_ref, _ = oracle.attn_exact(q, k, v, 0.125)
+    np.testing.assert_allclose(o, o_ref, atol=2e-5)
+    np.testing.assert_allclose(lse, lse_ref, atol=2e-4)
+
+
+@pytest.mark.parametrize("world", [3, 4, 5])
+def test_bidirectional_ring_on_gloo_matches_full_attention(world, tmp_path):
+    """Both-way rotation: every foreign block arrives once, odd and even rank counts."""
+    from blackflash_b200.inputs import make_qkv
+    from oracle import oracle
+    n = 128 * world
+    q, k, v = make_qkv(1, 2, n, dist="peaked", seed=20 + world)
+    q, k, v = (t.reshape(2, n, 64) for t in (q, k, v))
+    out = str(tmp_path / "ring2")
+    mp.spawn(_ring_worker, args=(world, _free_port(), q, k, v, out, "ring2"), nprocs=world, join=True)
     o = torch.cat([torch.load(f"{out}.{r}")["o"] for r in range(world)], dim=1).numpy()
     lse = torch.cat([torch.load(f"{out}.{r}")["lse"] for r in range(world)], dim=1).numpy()
     o_ref, lse_ref, _ = oracle.attn_exact(q, k, v, 0.125)

@@ -3,7 +3,7 @@
 Single GPU: the ring's compute - partial attention per KV block, log-sum-exp
 merge, bf16 cast - run over G blocks in one process must equal the full forward
 and the oracle. Two or more GPUs: the real schedule over NCCL (one process per
-GPU, P2P send/recv), checked against the oracle."""
+GPU, P2P send/recv; both-way rotation from 3 ranks up), checked against the oracle."""
 import math
 import os
 import socket
@@ -100,15 +100,18 @@ def _ring_worker(rank, world, port, qkv, out, mode="ring"):
     q, k, v = (t.cuda() for t in qkv)
     n = q.shape[1] // world
     sl = slice(rank * n, (rank + 1) * n)
-    fn = ring_attention if mode == "ring" else allgather_attention
-    o = fn(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125)
+    args = (q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125)
+    if mode == "allgather":
+        o = allgather_attention(*args)
+    else:
+        o = ring_attention(*args, bidirectional=(mode == "ring"))
     torch.save(o.cpu(), f"{out}.{rank}")
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
-@pytest.mark.parametrize("mode", ["ring", "allgather"])
+@pytest.mark.parametrize("mode", ["ring", "ring1", "allgather"])
 def test_ring_over_nccl(tmp_path, mode):
     from blackflash_b200.inputs import make_qkv
     world = min(torch.cuda.device_count(), 4)

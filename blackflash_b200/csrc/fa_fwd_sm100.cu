@@ -33,7 +33,7 @@
 // while the current item's last steps and epilogue run.
 //
 // Exponentials: p = 2^(s * scale * log2 e - m). Most run on MUFU (ex2); a fixed
-// share (kEmuPairs of 8 pairs) runs on the FMA pipe (exp2_poly_x2) so both
+// share (kEmuPairs of every kEmuPeriod pairs) runs on the FMA pipe (exp2_poly_x2) so both
 // pipes share the load. Arithmetic on pairs uses the sm_100 f32x2 forms.
 //
 // Every mbarrier wait is bounded (WaitCtl): a lost arrival sets a status
@@ -81,9 +81,14 @@ constexpr bool kLazyMax = BF_LAZY_MAX != 0;
 #define BF_DEFER_P 0
 #endif
 #ifndef BF_EMU_PAIRS
-#define BF_EMU_PAIRS 2
+#define BF_EMU_PAIRS 1
 #endif
-constexpr int kEmuPairs = BF_EMU_PAIRS;  // of every 8 exp2 pairs, how many run on the FMA pipe
+#ifndef BF_EMU_PERIOD
+#define BF_EMU_PERIOD 8
+#endif
+constexpr int kEmuPairs = BF_EMU_PAIRS;    // of every kEmuPeriod exp2 pairs, how many run on the FMA pipe
+constexpr int kEmuPeriod = BF_EMU_PERIOD;  // 8, 16 or 32 (a thread holds 32 pairs per step)
+static_assert(kEmuPeriod == 8 || kEmuPeriod == 16 || kEmuPeriod == 32, "kEmuPeriod must divide 32");
 
 // Shared-memory layout, offsets from a 1024-byte aligned base.
 constexpr int kOffQ = 0;                                  // [2 buffers][2 tiles]
@@ -329,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
 
                 // p = 2^(s * scale * log2 e - m): the argument is one packed FMA per pair;
-                // kEmuPairs of every 8 pairs take the FMA-pipe exp2, the rest MUFU ex2.
+                // kEmuPairs of every kEmuPeriod pairs take the FMA-pipe exp2, the rest MUFU ex2.
                 // Returns this thread's partial row sum; fills pk with bf16 pairs.
                 uint32_t pk[2][16];
                 auto exps = [&](float m_ref) -> float {
@@ -347,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 p2 = x2;  // perf experiment only: exponentials skipped, results are wrong
                             } else
 #endif
-                            if ((c & 7) < kEmuPairs) {
+                            if (((q * 16 + c) & (kEmuPeriod - 1)) < kEmuPairs) {
                                 p2 = exp2_poly_x2<kLazyMax>(x2);
                             } else {
                                 float x0, x1;

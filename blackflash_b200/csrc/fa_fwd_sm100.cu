@@ -64,7 +64,21 @@ constexpr int kSoftWarps = 16;                       // 8 per query tile, 4 per 
 // warpgroup) so setmaxnreg can move registers from the issuer warps to the softmax.
 constexpr int kThreads = kSoftWarps * 32 + (BF_REGSPLIT ? 4 : 3) * 32;  // + TMA producer, S issuer, PV issuer
 constexpr int kTileBytes = kBM * kD * 2;  // 16 KiB (Q, K, V or O tile, bf16)
+// BF_MMA_ROWSUM: the row sum l comes from the tensor core (an N=16 MMA of P against an
+// all-ones tile into TMEM after each PV) instead of FADDs in the softmax. The two tiles
+// then share one P buffer in TMEM to make room for the sum columns.
+#ifndef BF_MMA_ROWSUM
+#define BF_MMA_ROWSUM 0
+#endif
+constexpr bool kMmaRowSum = BF_MMA_ROWSUM != 0;
 constexpr int kTmemCols = 512;
+// TMEM columns: S_t at t*128; P_t (bf16, 64 columns) and O_t (fp32, 64 columns) after
+// them. With kMmaRowSum one P buffer serves both tiles and L_t (16 columns) follows O.
+constexpr int kColS = 0;
+constexpr int kColP = 2 * 128;
+constexpr int kColO = kColP + (BF_MMA_ROWSUM ? 1 : 2) * 64;
+constexpr int kColL = kColO + 2 * 64;
+static_assert(kColL + (BF_MMA_ROWSUM ? 32 : 0) <= kTmemCols, "TMEM columns");
 constexpr int kProducerWarp = 16;  // TMA producer
 constexpr int kSWarp = 17;         // issues S = Q K^T; owns the TMEM allocation
 constexpr int kPVWarp = 18;        // issues O += P V
@@ -80,6 +94,8 @@ constexpr bool kLazyMax = BF_LAZY_MAX != 0;
 #ifndef BF_DEFER_P
 #define BF_DEFER_P 0
 #endif
+static_assert(!(BF_MMA_ROWSUM && (BF_DEFER_P || BF_LAZY_MAX)), "BF_MMA_ROWSUM excludes BF_DEFER_P and BF_LAZY_MAX");
+
 #ifndef BF_EMU_PAIRS
 #define BF_EMU_PAIRS 1
 #endif
@@ -95,7 +111,8 @@ constexpr int kOffQ = 0;                                  // [2 buffers][2 tiles
 constexpr int kOffK = kOffQ + 2 * kQTiles * kTileBytes;   // [kStages]
 constexpr int kOffV = kOffK + kStages * kTileBytes;       // [kStages]
 constexpr int kOffO = kOffV + kStages * kTileBytes;       // [2 tiles] bf16 output staging
-constexpr int kOffBar = kOffO + kQTiles * kTileBytes;
+constexpr int kOffOnes = kOffO + kQTiles * kTileBytes;    // 2 KiB of bf16 1.0 (kMmaRowSum)
+constexpr int kOffBar = kOffOnes + (BF_MMA_ROWSUM ? 2048 : 0);
 
 struct Bars {
     uint64_t q_full[2];
@@ -234,6 +251,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         bars->abort_flag = 0;
         fence_barrier_init();
     }
+    if constexpr (kMmaRowSum) {
+        // bf16 1.0 everywhere: whatever element order the descriptor walks, B is all ones.
+        if (warp >= kSoftWarps) {
+            uint32_t* ones = reinterpret_cast<uint32_t*>(smem + kOffOnes);
+            for (int i = threadIdx.x - kSoftWarps * 32; i < 512; i += kThreads - kSoftWarps * 32) ones[i] = 0x3F803F80u;
+            fence_proxy_async_smem();
+        }
+    }
     if (warp == kProducerWarp && lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -270,15 +295,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int h = lane >> 4;  // column half
         const int row = quarter * 32 + sub * 16 + (lane & 15);  // row within the tile == TMEM lane
         const uint32_t lane_off = (uint32_t)(quarter * 32 + sub * 16) << 16;
-        const uint32_t tS = tmem + lane_off + (uint32_t)(t * kBN);
-        const uint32_t tP = tmem + lane_off + (uint32_t)(2 * kBN + t * kD);
-        const uint32_t tO = tmem + lane_off + (uint32_t)(2 * kBN + 2 * kD + t * kD);
+        const uint32_t tS = tmem + lane_off + (uint32_t)(kColS + t * kBN);
+        const uint32_t tP = tmem + lane_off + (uint32_t)(kColP + (kMmaRowSum ? 0 : t * kD));
+        const uint32_t tO = tmem + lane_off + (uint32_t)(kColO + t * kD);
+        const uint32_t tL = tmem + lane_off + (uint32_t)(kColL + t * 16);  // kMmaRowSum only
         const float sl2 = p.scale_log2;
         const uint64_t sl2_2 = f2_pack(sl2, sl2);
         const uint32_t bar_s = smem_addr(&bars->s_full[t]);
         const uint32_t bar_se = smem_addr(&bars->s_empty[t]);
         const uint32_t bar_p = smem_addr(&bars->p_full[t]);
         const uint32_t bar_pv = smem_addr(&bars->pv_done[t]);
+        // The PV that reads P last before this tile rewrites it: its own previous one, or
+        // with the shared P buffer the other tile's (tile 0 waits PV_1(g-1), tile 1 PV_0(g)).
+        // Commits cover all earlier MMAs of the issuing thread, so either wait also
+        // guarantees this tile's own PV(g-1) (O and L final before a rescale).
+        const uint32_t bar_preuse = smem_addr(&bars->pv_done[kMmaRowSum ? 1 - t : t]);
         const bool issuer = (warp & 7) == 0 && lane == 0;  // issues tile t's TMA stores
         const bool tracing = trace_hit && issuer;
         uint8_t* stage = smem + kOffO + t * kTileBytes;
@@ -359,10 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 f2_unpack(x2, x0, x1);
                                 p2 = f2_pack(fast_exp2(x0), fast_exp2(x1));
                             }
-                            if (c & 1)
-                                sum_b = f2_add(sum_b, p2);
-                            else
-                                sum_a = f2_add(sum_a, p2);
+                            if constexpr (!kMmaRowSum) {
+                                if (c & 1)
+                                    sum_b = f2_add(sum_b, p2);
+                                else
+                                    sum_a = f2_add(sum_a, p2);
+                            }
                             float p0, p1;
                             f2_unpack(p2, p0, p1);
                             pk[q][c] = pack_bf16x2(p0, p1);
@@ -400,7 +433,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         alpha = fast_exp2(m_use - m_new);  // 0 on the first tile
                         m_use = m_new;
                     }
-                    l_half = l_half * alpha + exps(m_use);
+                    if constexpr (kMmaRowSum)
+                        exps(m_use);
+                    else
+                        l_half = l_half * alpha + exps(m_use);
                 } else {
                     // The tile max is computed only on a slice's first tile (or when row_max
                     // is requested). Later tiles use the reference max directly and check the
@@ -442,8 +478,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
                 // P_t of the previous step must have been consumed (and O_t be final)
                 // before we overwrite P_t / rescale O_t.
-                if (g > 0 && !kPerfDecouple) {
-                    if (!(ok = warp_wait(bar_pv, (g - 1) & 1u, ctl, kSiteSoftPV))) break;
+                if (kMmaRowSum && t == 1 && !kPerfDecouple) {
+                    if (!(ok = warp_wait(bar_preuse, g & 1u, ctl, kSiteSoftPV))) break;
+                    tc_fence_after();
+                } else if (g > 0 && !kPerfDecouple) {
+                    if (!(ok = warp_wait(bar_preuse, (g - 1) & 1u, ctl, kSiteSoftPV))) break;
                     tc_fence_after();
                 }
                 BF_TRACE(t, g, 5);
@@ -454,6 +493,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
                     tmem_st16x32bx2_x32<32>(tO, o);
+                    if constexpr (kMmaRowSum) {
+                        const uint32_t lv = tmem_ld16x32bx2_x1<8>(tL);
+                        tmem_wait_ld();
+                        tmem_st16x32bx2_x1<8>(tL, __float_as_uint(__uint_as_float(lv) * alpha));
+                    }
                 }
                 // bf16 P: this thread's 64 S columns are P columns 32h + [0, 32).
                 tmem_st16x32bx2_x16<32>(tP, pk[0]);
@@ -482,8 +526,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             uint32_t o[32];
             tmem_ld16x32bx2_x32<32>(tO, o);
-            tmem_wait_ld();
-            const float l_sum = l_half + __shfl_xor_sync(0xffffffffu, l_half, 16);
+            float l_sum;
+            if constexpr (kMmaRowSum) {
+                l_sum = __uint_as_float(tmem_ld16x32bx2_x1<8>(tL));  // every L column holds the row sum
+                tmem_wait_ld();
+            } else {
+                tmem_wait_ld();
+                l_sum = l_half + __shfl_xor_sync(0xffffffffu, l_half, 16);
+            }
             const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
             const int q_row = q_row0 + t * kBM + row;
             const bool row_ok = q_row < p.n_q;
@@ -602,6 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // busy softmax warps, and the tensor core's issue queue is shallow.
         constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);  // Q (K-major) x K (K-major)
         constexpr uint32_t kIdescO = idesc_bf16_f32(kBM, kD, 1);   // P (TMEM)   x V (MN-major)
+        constexpr uint32_t kIdescL = idesc_bf16_f32(kBM, 16, 1);   // P (TMEM)   x ones (N = 16)
         const bool leader = elect_one();
         const bool tracing = trace_hit && leader;
         const uint64_t desc_base = smem_desc_sw128(smem_addr(smem), 16, 1024);
@@ -609,6 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t desc_lo0 = (uint32_t)desc_base;  // low word of a descriptor at smem offset 0
         constexpr uint32_t kTileLo = kTileBytes >> 4;   // low-word step between 16 KiB tiles
         const uint32_t q_lo0 = desc_lo0 + (kOffQ >> 4), k_lo0 = desc_lo0 + (kOffK >> 4), v_lo0 = desc_lo0 + (kOffV >> 4);
+        const uint32_t ones_lo = desc_lo0 + (kOffOnes >> 4);
         const uint32_t q_full0 = smem_addr(&bars->q_full[0]), q_empty0 = smem_addr(&bars->q_empty[0]);
         const uint32_t k_full0 = smem_addr(&bars->k_full[0]), k_empty0 = smem_addr(&bars->k_empty[0]);
         const uint32_t v_full0 = smem_addr(&bars->v_full[0]), v_empty0 = smem_addr(&bars->v_empty[0]);
@@ -649,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint32_t q_lo = q_lo0 + (uint32_t)(qb * kQTiles + t) * kTileLo;
 #pragma unroll
                             for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements = 32 B inside the swizzle atom
-                                umma_ss_lo(tmem + t * kBN, q_lo + kk * 2, k_lo + kk * 2, desc_hi, kIdescS, kk > 0);
+                                umma_ss_lo(tmem + kColS + t * kBN, q_lo + kk * 2, k_lo + kk * 2, desc_hi, kIdescS, kk > 0);
                             umma_commit(s_full0 + 8 * t);
                         }
                         __syncwarp();
@@ -672,10 +724,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_fence_after();
                         BF_TRACE(2, g, 6 + t);  // PV_t(g) issue starts
                         if (leader) {
+                            const uint32_t p_col = tmem + kColP + (kMmaRowSum ? 0 : t * kD);
 #pragma unroll
                             for (int kk = 0; kk < kBN / 16; ++kk)  // 16 KV rows: 8 TMEM columns of P, 16 x 128 B of V
-                                umma_ts_lo(tmem + 2 * kBN + 2 * kD + t * kD, tmem + 2 * kBN + t * kD + kk * 8,
-                                           v_lo + kk * 128, desc_hi, kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+                                umma_ts_lo(tmem + kColO + t * kD, p_col + kk * 8, v_lo + kk * 128, desc_hi, kIdescO,
+                                           (j > 0 || kk > 0) ? 1u : 0u);
+                            if constexpr (kMmaRowSum) {
+                                // L_t += P 1: every K step reads the same 2 KiB of ones.
+#pragma unroll
+                                for (int kk = 0; kk < kBN / 16; ++kk)
+                                    umma_ts_lo(tmem + kColL + t * 16, p_col + kk * 8, ones_lo, desc_hi, kIdescL,
+                                               (j > 0 || kk > 0) ? 1u : 0u);
+                            }
                             umma_commit(pv_done0 + 8 * t);
                         }
                         __syncwarp();

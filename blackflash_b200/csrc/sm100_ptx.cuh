@@ -286,6 +286,19 @@ __device__ __forceinline__ void tmem_st16x32bx2_x16(uint32_t taddr, const uint32
         : "memory");
 }
 
+// One column per thread: threads 0-15 read column 0 of lanes base..base+15,
+// threads 16-31 column SPLIT of the same lanes.
+template <int SPLIT>
+__device__ __forceinline__ uint32_t tmem_ld16x32bx2_x1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.16x32bx2.x1.b32 {%0}, [%1], %2;" : "=r"(r) : "r"(taddr), "n"(SPLIT));
+    return r;
+}
+template <int SPLIT>
+__device__ __forceinline__ void tmem_st16x32bx2_x1(uint32_t taddr, uint32_t r) {
+    asm volatile("tcgen05.st.sync.aligned.16x32bx2.x1.b32 [%0], %2, {%1};" ::"r"(taddr), "r"(r), "n"(SPLIT) : "memory");
+}
+
 // 16 columns variant (used for the bf16 P tile: 128 bf16 = 64 columns = 4 x 16).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
     asm volatile(

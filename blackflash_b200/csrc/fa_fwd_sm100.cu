@@ -769,6 +769,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+#include "fa_fwd_sm100_d128.cuh"
+
 }  // namespace bfk
 
 // ============================================================================ host side
@@ -792,11 +794,12 @@ PFN_encodeTiled get_encode_fn() {
 
 // [BH][rows][64] bf16 viewed as a 3-D tensor; 64 x 128-row boxes with 128-byte
 // swizzle. Rows past `rows` inside a slice load as zero and are never stored.
-int make_map(CUtensorMap* m, const void* base, long long bh, int rows) {
+// For d = 128 the same 64-column box is loaded twice per tile (columns 0 and 64).
+int make_map(CUtensorMap* m, const void* base, long long bh, int rows, int d = bfk::kD) {
     PFN_encodeTiled enc = get_encode_fn();
     if (!enc) return bf_set_error(BF_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    cuuint64_t dims[3] = {(cuuint64_t)bfk::kD, (cuuint64_t)rows, (cuuint64_t)bh};
-    cuuint64_t strides[2] = {(cuuint64_t)bfk::kD * 2, (cuuint64_t)rows * bfk::kD * 2};
+    cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)bh};
+    cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)rows * d * 2};
     cuuint32_t box[3] = {(cuuint32_t)bfk::kD, (cuuint32_t)bfk::kBM, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
@@ -838,7 +841,7 @@ int sm_count(int* out) {
 
 int bf_fwd_launch(const BfFwdArgs* a) {
     int rc0;
-    if (a->d != bfk::kD) return bf_set_error(BF_ERR_ARG, "BlackFlash currently only supports d=64");
+    if (a->d != bfk::kD && a->d != bfk::d128::kD) return bf_set_error(BF_ERR_ARG, "BlackFlash supports d=64 and d=128");
     if (a->bh <= 0 || a->n_q <= 0 || a->n_kv <= 0) return bf_set_error(BF_ERR_ARG, "empty problem: B*H and N must be >= 1");
     if (!a->q || !a->k || !a->v || (!a->o && !a->o_f32)) return bf_set_error(BF_ERR_ARG, "null tensor pointer");
     auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
@@ -854,6 +857,42 @@ int bf_fwd_launch(const BfFwdArgs* a) {
 
     CUtensorMap mq, mk, mv, mo;
     int rc;
+    if (a->d == bfk::d128::kD) {
+        if (!a->o || a->o_f32 || a->kv_blocks || a->trace || a->dbg_s || a->skip_k_loads)
+            return bf_set_error(BF_ERR_ARG, "d=128 supports the bf16 forward (causal, lse and row max optional) only");
+        if ((rc = make_map(&mq, a->q, a->bh, a->n_q, 128)) != BF_OK) return rc;
+        if ((rc = make_map(&mk, a->k, a->bh, a->n_kv, 128)) != BF_OK) return rc;
+        if ((rc = make_map(&mv, a->v, a->bh, a->n_kv, 128)) != BF_OK) return rc;
+        bfk::KParams kp;
+        memset(&kp, 0, sizeof(kp));
+        kp.n_q = a->n_q;
+        kp.n_kv = a->n_kv;
+        kp.q_blocks = (int)q_blocks;
+        kp.items = (int)items;
+        kp.scale = a->scale;
+        kp.scale_log2 = a->scale * 1.4426950408889634f;
+        kp.lse = a->lse;
+        kp.row_max = a->row_max;
+        kp.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
+        kp.causal = a->causal;
+        kp.kv_skip = -1;
+        kp.bh_count = (int)a->bh;
+        static bool done[64] = {false};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
+        if (!done[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(bfk::d128::fa_fwd_d128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 bfk::d128::kSmemBytes);
+            if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
+            done[dev] = true;
+        }
+        bfk::d128::fa_fwd_d128_kernel<<<(unsigned)grid, bfk::kThreads, bfk::d128::kSmemBytes,
+                                       reinterpret_cast<cudaStream_t>(a->stream)>>>(
+            mq, mk, mv, reinterpret_cast<__nv_bfloat16*>(a->o), kp);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
+        return BF_OK;
+    }
     if ((rc = make_map(&mq, a->q, a->bh, a->n_q)) != BF_OK) return rc;
     int kv_blk_tiles = 0;
     if (a->kv_blocks) {

@@ -2,7 +2,7 @@
 
 `forward` mirrors the reference's torch extension function
 `blackflash_cuda.forward` (binding/blackflash_ops.cu:18-55): same argument
-order and meaning, same checks (CUDA, bf16, contiguous, d == 64), the same
+order and meaning, same checks (CUDA, bf16, contiguous, d == 64; d == 128 is accepted as an extension), the same
 RuntimeError on a failed check, and a fresh bf16 O as the result. What differs:
   * it launches on Q's device (the reference has no device guard and uses
     whatever device is current);
@@ -32,7 +32,7 @@ def _check_qkv(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor) -> None:
         _require(t.dim() == 4, f"{name} must be [B, H, N, d]")
     _require(K.shape == Q.shape and V.shape == Q.shape, "Q, K and V must have the same shape")
     _require(K.device == Q.device and V.device == Q.device, "Q, K and V must be on the same device")
-    _require(Q.size(3) == 64, "BlackFlash currently only supports d=64")
+    _require(Q.size(3) in (64, 128), "BlackFlash supports d=64 and d=128")
 
 
 def _stream_handle(dev: torch.device) -> int:
@@ -40,7 +40,7 @@ def _stream_handle(dev: torch.device) -> int:
 
 
 def forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float) -> torch.Tensor:
-    """O = softmax(scale * Q K^T) V; bf16 [B, H, N, 64] in and out."""
+    """O = softmax(scale * Q K^T) V; bf16 [B, H, N, d] in and out, d = 64 or 128."""
     return forward_lse(Q, K, V, scale, want_stats=False)[0]
 
 
@@ -78,7 +78,7 @@ def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float,
 def blackflash(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float | None = None,
                causal: bool = False) -> torch.Tensor:
     """Attention forward. Mirrors the reference's Python API (blackflash/__init__.py:5-18):
-    Q, K, V are [B, H, N, d] bf16 CUDA tensors with d == 64; scale defaults to 1/sqrt(d).
+    Q, K, V are [B, H, N, d] bf16 CUDA tensors with d == 64 (the reference's only size) or 128; scale defaults to 1/sqrt(d).
     `causal` (default False, the reference's only mode) is an extension."""
     if scale is None:
         scale = 1.0 / math.sqrt(Q.size(-1))
@@ -178,7 +178,7 @@ def blackflash_host(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: fl
         _require(not t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.dim() == 4,
                  f"{name} must be a contiguous host bf16 [B, H, N, d] tensor")
     _require(K.shape == Q.shape and V.shape == Q.shape, "Q, K and V must have the same shape")
-    _require(Q.size(3) == 64, "BlackFlash currently only supports d=64")
+    _require(Q.size(3) in (64, 128), "BlackFlash supports d=64 and d=128")
     B, H, N, d = Q.shape
     if scale is None:
         scale = 1.0 / math.sqrt(d)

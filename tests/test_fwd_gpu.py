@@ -153,9 +153,9 @@ def test_input_checks_raise():
         forward(q.cpu(), q, q, 0.125)
     with pytest.raises(RuntimeError):
         forward(q.transpose(2, 3), q, q, 0.125)
-    q128 = torch.randn(1, 1, 64, 128, device=_dev(), dtype=torch.bfloat16)
+    q96 = torch.randn(1, 1, 64, 96, device=_dev(), dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="d=64"):
-        blackflash(q128, q128, q128)
+        blackflash(q96, q96, q96)
 
 
 def test_empty_input_returns_empty():

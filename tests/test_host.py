@@ -47,7 +47,7 @@ def test_argument_errors_without_device_work():
     """Invalid arguments are rejected by the library before any CUDA call."""
     from blackflash_b200 import _lib
     lib = _lib.load()
-    rc = lib.blackflash_fwd(16, 16, 16, 16, None, None, 1, 1, 64, 128, 0.125, None)
+    rc = lib.blackflash_fwd(16, 16, 16, 16, None, None, 1, 1, 64, 96, 0.125, None)
     assert rc == _lib.BF_ERR_ARG and b"d=64" in lib.blackflash_last_error()
     rc = lib.blackflash_fwd(16, 16, 16, 16, None, None, 0, 1, 64, 64, 0.125, None)
     assert rc == _lib.BF_ERR_ARG

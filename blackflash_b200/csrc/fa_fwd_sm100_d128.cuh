@@ -33,6 +33,7 @@ constexpr int kOffK = kOffQ + kQTiles * kTileBytes;      // [kStages][2 chunks]
 constexpr int kOffV = kOffK + kStages * kTileBytes;      // [kStages][2 chunks]
 constexpr int kOffBar = kOffV + kStages * kTileBytes;
 constexpr int kColO = 2 * kBN;                           // O_t at 256 + 128 t
+constexpr int kHalfN = 64;                               // S is issued as two N = 64 halves
 
 struct Bars {
     uint64_t q_full[kQTiles];
@@ -42,6 +43,7 @@ struct Bars {
     uint64_t v_full[kStages];
     uint64_t v_empty[kStages];
     uint64_t s_full[kQTiles];
+    uint64_t s_empty[kQTiles];
     uint64_t p_full[kQTiles];
     uint64_t pv_done[kQTiles];
     uint64_t drain;
@@ -57,7 +59,7 @@ enum : unsigned {
     kSiteProdK = 0x501,
     kSiteProdV = 0x502,
     kSiteMmaQ = 0x510,  // + t
-    kSiteMmaK = 0x520,  // +0 K full, +1 + t PV_t(g-1) done
+    kSiteMmaK = 0x520,  // +0 K full, +1 + t PV_t(g-1) done, +3 + t S_t(g-1) loaded
     kSiteMmaV = 0x530,  // +0 V full, +1 + t P_t full
     kSiteSoftS = 0x540,
     kSiteSoftO = 0x541,
@@ -78,6 +80,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_addr(&bars->q_full[t]), 1);
             mbar_init(smem_addr(&bars->q_empty[t]), 1);
             mbar_init(smem_addr(&bars->s_full[t]), 1);
+            mbar_init(smem_addr(&bars->s_empty[t]), 2 * kBM);
             mbar_init(smem_addr(&bars->p_full[t]), 2 * kBM);
             mbar_init(smem_addr(&bars->pv_done[t]), 1);
         }
@@ -129,6 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = p.scale_log2;
         const uint64_t sl2_2 = f2_pack(sl2, sl2);
         const uint32_t bar_s = smem_addr(&bars->s_full[t]);
+        const uint32_t bar_se = smem_addr(&bars->s_empty[t]);
         const uint32_t bar_p = smem_addr(&bars->p_full[t]);
         const uint32_t bar_pv = smem_addr(&bars->pv_done[t]);
         uint32_t g = 0;
@@ -149,6 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld16x32bx2_x32<64>(tS + 0, s[0]);
                 tmem_ld16x32bx2_x32<64>(tS + 32, s[1]);
                 tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(bar_se);  // S_t is in registers: its upper 64 columns may be rewritten
 
                 const int q_abs = q_row0 + t * kBM + row;
                 const int kv_lim = p.causal ? min(p.n_kv, q_abs + 1) : p.n_kv;
@@ -333,7 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (warp == kSWarp || warp == kPVWarp) {
         // ------------------------------------------------------------ MMA issuers
-        constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);     // Q (K-major) x K (K-major)
+        constexpr uint32_t kIdescSh = idesc_bf16_f32(kBM, kHalfN, 0);  // Q (K-major) x 64 K rows (K-major)
+        constexpr uint32_t kHalfRowsLo = (64 * 128) >> 4;             // K rows 64.. inside a chunk
         constexpr uint32_t kIdescO = idesc_bf16_f32(kBM, kChunk, 1);  // P (TMEM)   x V chunk (MN-major)
         const bool leader = elect_one();
         const uint64_t desc_base = smem_desc_sw128(smem_addr(smem), 16, 1024);
@@ -364,17 +371,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 break;
                             tc_fence_after();
                         }
-                        if (g > 0) {  // P_t(g-1), aliased in S_t, has been read by PV_t(g-1)
+                        const uint32_t q_lo = q_lo0 + (uint32_t)t * kTileLo;
+                        // Upper half (keys 64..127 -> S_t columns 64..127): free once the
+                        // softmax has loaded S_t(g-1).
+                        if (g > 0) {
+                            if (!(ok = warp_wait(smem_addr(&bars->s_empty[t]), (g - 1) & 1u, ctl, kSiteMmaK + 3 + t)))
+                                break;
+                            tc_fence_after();
+                        }
+                        if (leader) {
+#pragma unroll
+                            for (int kk = 0; kk < kD / 16; ++kk) {
+                                const uint32_t off = (uint32_t)(kk >> 2) * kChunkLo + (uint32_t)(kk & 3) * 2;
+                                umma_ss_lo(tmem + t * kBN + kHalfN, q_lo + off, k_lo + off + kHalfRowsLo, desc_hi,
+                                           kIdescSh, kk > 0);
+                            }
+                        }
+                        __syncwarp();
+                        // Lower half (keys 0..63 -> columns 0..63, where P_t(g-1) lives):
+                        // after PV_t(g-1) has read P.
+                        if (g > 0) {
                             if (!(ok = warp_wait(smem_addr(&bars->pv_done[t]), (g - 1) & 1u, ctl, kSiteMmaK + 1 + t)))
                                 break;
                             tc_fence_after();
                         }
                         if (leader) {
-                            const uint32_t q_lo = q_lo0 + (uint32_t)t * kTileLo;
 #pragma unroll
                             for (int kk = 0; kk < kD / 16; ++kk) {
                                 const uint32_t off = (uint32_t)(kk >> 2) * kChunkLo + (uint32_t)(kk & 3) * 2;
-                                umma_ss_lo(tmem + t * kBN, q_lo + off, k_lo + off, desc_hi, kIdescS, kk > 0);
+                                umma_ss_lo(tmem + t * kBN, q_lo + off, k_lo + off, desc_hi, kIdescSh, kk > 0);
                             }
                             umma_commit(smem_addr(&bars->s_full[t]));
                             if (j == nk_item - 1) umma_commit(smem_addr(&bars->q_empty[t]));

@@ -34,6 +34,12 @@ constexpr int kOffV = kOffK + kStages * kTileBytes;      // [kStages][2 chunks]
 constexpr int kOffBar = kOffV + kStages * kTileBytes;
 constexpr int kColO = 2 * kBN;                           // O_t at 256 + 128 t
 constexpr int kHalfN = 64;                               // S is issued as two N = 64 halves
+// At d = 128 the tensor core carries twice the work per exponential, so MUFU has
+// headroom and the FMA-pipe exp2 only costs issue slots: measured best at 0 of 8.
+#ifndef BF_EMU_PAIRS_D128
+#define BF_EMU_PAIRS_D128 0
+#endif
+constexpr int kEmuPairs128 = BF_EMU_PAIRS_D128;          // FMA-pipe exp2 pairs of every kEmuPeriod
 
 struct Bars {
     uint64_t q_full[kQTiles];
@@ -192,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t x2 =
                             f2_fma(f2_pack(__uint_as_float(s[q][2 * c]), __uint_as_float(s[q][2 * c + 1])), sl2_2, negm_2);
                         uint64_t p2;
-                        if (((q * 16 + c) & (kEmuPeriod - 1)) < kEmuPairs) {
+                        if (((q * 16 + c) & (kEmuPeriod - 1)) < kEmuPairs128) {
                             p2 = exp2_poly_x2<false>(x2);
                         } else {
                             float x0, x1;

@@ -47,6 +47,8 @@ CONFIGS = {
     "5": (1, 32, 65536, 64, "normal"),
     # profiling case: same per-slice shape as config 3, 1/4 of the slices (1.6 GB device memory)
     "prof": (16, 64, 1024, 64, "normal"),
+    # head dimension 128 (extension; the reference kernel is d = 64 only)
+    "d128": (16, 16, 4096, 128, "normal"),
 }
 METRIC = "attention fwd TFLOPS (4BHN^2d/t)"
 
@@ -305,13 +307,13 @@ def run_ours(args, cfg_name):
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal, scale 1/8",
+            "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal, scale 1/sqrt({d})",
                        "global_batch": B, "seq_len": N, "parallelism": f"bxh{world} (no collective)",
                        "l2": "inputs larger than L2 (no flush)", "slices_per_rank": my},
             "roofline": {"bound": "tensor", "achieved": per_gpu_achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": per_gpu_achieved / peak if peak else None, "traffic": traffic,
                          "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
-                         "kernel": "fa_fwd_sm100_kernel", "flops_per_launch": f_rank},
+                         "kernel": "fa_fwd_sm100_kernel" if d == 64 else "fa_fwd_d128_kernel", "flops_per_launch": f_rank},
             "cpu_baseline": cpu,
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": bytes_in,

@@ -1,5 +1,5 @@
 /*
- * BlackFlash-B200 C ABI: attention forward (non-causal, bf16, head dim 64) on
+ * BlackFlash-B200 C ABI: attention forward (non-causal, bf16, head dim 64, or 128 as an extension) on
  * sm_100a.
  *
  * Every entry point takes plain device pointers, sizes and a cudaStream_t passed
@@ -8,7 +8,7 @@
  * thread. No entry point allocates device memory or synchronises the device,
  * except the ones documented as synchronous (blackflash_status).
  *
- * Layouts: Q, K, V and O are contiguous [B, H, N, 64] bf16 (the same layout as
+ * Layouts: Q, K, V and O are contiguous [B, H, N, d] bf16, d = 64 or 128 (the same layout as
  * the reference, binding/blackflash_ops.cu:24-27). lse and row_max are [B, H, N]
  * fp32.
  */
@@ -34,7 +34,7 @@ extern "C" {
  * The reference documents those two slots but never writes them.
  *   lse[b,h,i]     = log(sum_j exp(scale * S_ij))   (natural log)
  *   row_max[b,h,i] = max_j scale * S_ij
- * Requirements: d == 64, B, H, N >= 1, every pointer 16-byte aligned.
+ * Requirements: d == 64 (reference) or 128 (blackflash_fwd, blackflash_fwd_causal), B, H, N >= 1, every pointer 16-byte aligned.
  * N need not be a multiple of 128: the kernel masks the ragged KV tile and
  * skips stores past row N.
  */

@@ -5,7 +5,7 @@
 //
 // Arguments: Q, K, V, O are [B, H, N, d] bf16 device tensors; l and m are
 // [B, H, N] fp32 and receive the logsumexp and the row max of scale*QK^T
-// (either may be null); d must be 64. The call is asynchronous on `stream`.
+// (either may be null); d must be 64 (or 128, an extension). The call is asynchronous on `stream`.
 // Unlike the reference it never calls exit(): on an error it prints the
 // message to stderr and leaves it in blackflash_last_error() (blackflash_b200.h).
 #pragma once

@@ -9,6 +9,9 @@ Contents:
                accumulated in double. Returns O, lse and the row max in fp32.
   attn_fa2     the C restatement of the reference kernel's tiled online-softmax
                algorithm (kernel/flash_attn_mma.cu:228-464). Returns a bf16-rounded O.
+  attn_bwd     gradients dQ, dK, dV of the same forward for an upstream dO, in double
+               (attn_bwd_oracle.c; the reference has no backward, so it is pinned
+               against torch autograd of the fp32 forward instead).
   scores       S = QK^T * scale and P = softmax(S) of one slice, which is what
                gen_ref.py saves as s_ref.bin / p_ref.bin (:80-84).
   attn_numpy   a float64 numpy statement of the same formula, used to cross-check
@@ -30,8 +33,8 @@ _lib = None
 
 
 def build() -> str:
-    src = os.path.join(HERE, "attn_oracle.c")
-    if not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(src):
+    srcs = [os.path.join(HERE, f) for f in ("attn_oracle.c", "attn_bwd_oracle.c")]
+    if not os.path.exists(LIB) or any(os.path.getmtime(LIB) < os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", HERE, "all"], check=True, capture_output=True)
     return LIB
 
@@ -46,6 +49,8 @@ def _load():
         lib.oracle_attn_exact_causal.restype = i
         lib.oracle_attn_fa2.argtypes = [vp, vp, vp, vp, vp, vp, ll, i, i, f, i]
         lib.oracle_scores.argtypes = [vp, vp, vp, vp, i, i, f]
+        lib.oracle_attn_bwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, ll, i, i, f, i]
+        lib.oracle_attn_bwd.restype = i
         for fn in (lib.oracle_attn_exact, lib.oracle_attn_fa2, lib.oracle_scores):
             fn.restype = i
         _lib = lib
@@ -100,6 +105,18 @@ def attn_fa2(q, k, v, scale: float, nthreads: int | None = None):
     _load().oracle_attn_fa2(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(o), _ptr(lse), _ptr(mx), bh, n, d, float(scale),
                             nthreads or os.cpu_count() or 1)
     return o, lse, mx
+
+
+def attn_bwd(q, k, v, dout, scale: float, nthreads: int | None = None):
+    """Gradients of O = softmax(scale Q K^T) V for upstream dO, all bf16 [..., N, d].
+    Returns (dQ, dK, dV) fp32 numpy, computed in double (attn_bwd_oracle.c)."""
+    qb, kb, vb, gb = as_bf16_bits(q), as_bf16_bits(k), as_bf16_bits(v), as_bf16_bits(dout)
+    *lead, n, d = qb.shape
+    bh = int(np.prod(lead)) if lead else 1
+    dq, dk, dv = (np.empty(qb.shape, dtype=np.float32) for _ in range(3))
+    _load().oracle_attn_bwd(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(gb), _ptr(dq), _ptr(dk), _ptr(dv), bh, n, d,
+                            float(scale), nthreads or os.cpu_count() or 1)
+    return dq, dk, dv
 
 
 def scores(q_slice, k_slice, scale: float):

@@ -84,3 +84,21 @@ def test_causal_exact_vs_numpy(shape):
     o64, lse64 = oracle.attn_numpy(q, k, v, 0.125, causal=True)
     np.testing.assert_allclose(o, o64, atol=1e-6, rtol=1e-6)
     np.testing.assert_allclose(lse, lse64, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,H,N,d", [(1, 2, 64, 64), (2, 1, 100, 64), (1, 1, 37, 128)])
+def test_backward_oracle_matches_torch_autograd(B, H, N, d):
+    """The backward restatement against autograd of the fp32 math forward
+    (reference tests/test_blackflash.py:16-19) on the same bf16 inputs."""
+    import torch
+    from blackflash_b200.inputs import make_qkv
+    q, k, v = make_qkv(B, H, N, d=d, dist="normal", seed=N + d)
+    g = torch.Generator().manual_seed(3)
+    do = torch.randn(q.shape, generator=g).to(torch.bfloat16)
+    scale = 1.0 / d ** 0.5
+    qf, kf, vf = (t.double().requires_grad_(True) for t in (q, k, v))
+    o = torch.softmax((qf @ kf.transpose(-1, -2)) * scale, dim=-1) @ vf
+    o.backward(do.double())
+    dq, dk, dv = oracle.attn_bwd(q, k, v, do, scale)
+    for got, ref in ((dq, qf.grad), (dk, kf.grad), (dv, vf.grad)):
+        np.testing.assert_allclose(got, ref.numpy(), rtol=1e-5, atol=1e-6)

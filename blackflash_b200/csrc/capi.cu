@@ -84,6 +84,39 @@ extern "C" int blackflash_fwd_partial(const void* Q, const void* K, const void* 
     return bf_fwd_launch(&a);
 }
 
+extern "C" long long blackflash_bwd_workspace_bytes(int B, int H, int N, int d) {
+    if (B <= 0 || H <= 0 || N <= 0 || d != 64) return 0;
+    return bf_bwd_workspace_bytes((long long)B * H, N);
+}
+
+extern "C" int blackflash_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                              const float* lse, void* dQ, void* dK, void* dV, void* workspace,
+                              long long workspace_bytes, int B, int H, int N, int d, float scale, void* stream) {
+    g_last_error[0] = 0;
+    if (check_bhn(B, H, N) != BF_OK) return BF_ERR_ARG;
+    if (d != 64) return bf_set_error(BF_ERR_ARG, "the backward supports d=64");
+    if (workspace_bytes < bf_bwd_workspace_bytes((long long)B * H, N))
+        return bf_set_error(BF_ERR_ARG, "workspace smaller than blackflash_bwd_workspace_bytes()");
+    BfBwdArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = Q;
+    a.k = K;
+    a.v = V;
+    a.o = O;
+    a.dout = dO;
+    a.lse = lse;
+    a.dq = dQ;
+    a.dk = dK;
+    a.dv = dV;
+    a.workspace = workspace;
+    a.bh = (long long)B * H;
+    a.n = N;
+    a.d = d;
+    a.scale = scale;
+    a.stream = stream;
+    return bf_bwd_launch(&a);
+}
+
 extern "C" int blackflash_fwd_partial_blocks(const void* Q, const void* Kg, const void* Vg, float* O_f32, float* lse,
                                              long long BH, int Nq, int n_blocks, int block_rows, int skip, int d,
                                              float scale, void* stream) {

@@ -770,6 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 #include "fa_fwd_sm100_d128.cuh"
+#include "fa_bwd_sm100.cuh"
 
 }  // namespace bfk
 
@@ -798,6 +799,12 @@ PFN_encodeTiled get_encode_fn() {
 int make_map(CUtensorMap* m, const void* base, long long bh, int rows, int d = bfk::kD) {
     PFN_encodeTiled enc = get_encode_fn();
     if (!enc) return bf_set_error(BF_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    // The encode is a driver call and needs a current context. A thread that has only
+    // used the runtime implicitly (torch's autograd worker, for one) may not have one
+    // yet; cudaSetDevice makes the device's primary context current.
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess || cudaSetDevice(cur) != cudaSuccess)
+        return bf_set_error(BF_ERR_CUDA, "no CUDA device context");
     cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)bh};
     cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)rows * d * 2};
     cuuint32_t box[3] = {(cuuint32_t)bfk::kD, (cuuint32_t)bfk::kBM, 1};
@@ -805,7 +812,12 @@ int make_map(CUtensorMap* m, const void* base, long long bh, int rows, int d = b
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return bf_set_error(BF_ERR_CUDA, "cuTensorMapEncodeTiled rejected the tensor");
+    if (r != CUDA_SUCCESS) {
+        char msg[200];
+        snprintf(msg, sizeof(msg), "cuTensorMapEncodeTiled rejected the tensor (error %d, base %p, rows %d, slices %lld, d %d)",
+                 (int)r, base, rows, bh, d);
+        return bf_set_error(BF_ERR_CUDA, msg);
+    }
     return BF_OK;
 }
 
@@ -955,6 +967,91 @@ int bf_fwd_launch(const BfFwdArgs* a) {
         bfk::fa_fwd_sm100_kernel<false><<<(unsigned)grid, bfk::kThreads, bfk::kSmemBytes, stream>>>(mq, mk, mv, mo, kp);
     }
     const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
+    return BF_OK;
+}
+
+long long bf_bwd_workspace_bytes(long long bh, int n) {
+    const long long n_pad = ((long long)n + 127) / 128 * 128;
+    return 4LL * (bh * n * 64 + 2 * bh * n_pad);
+}
+
+int bf_bwd_launch(const BfBwdArgs* a) {
+    if (a->d != bfk::kD) return bf_set_error(BF_ERR_ARG, "the backward supports d=64");
+    if (a->bh <= 0 || a->n <= 0) return bf_set_error(BF_ERR_ARG, "empty problem: B*H and N must be >= 1");
+    const void* ptrs[] = {a->q, a->k, a->v, a->o, a->dout, a->lse, a->dq, a->dk, a->dv, a->workspace};
+    for (const void* ptr : ptrs) {
+        if (!ptr) return bf_set_error(BF_ERR_ARG, "null pointer");
+        if (reinterpret_cast<uintptr_t>(ptr) & 15u) return bf_set_error(BF_ERR_ARG, "every pointer must be 16-byte aligned");
+    }
+    const long long q_tiles = ((long long)a->n + 127) / 128;
+    const long long blocks = q_tiles * a->bh;
+    if (blocks > 0x7fffffffLL) return bf_set_error(BF_ERR_ARG, "problem too large for one launch");
+    const int n_pad = (int)(q_tiles * 128);
+    float* dq_acc = reinterpret_cast<float*>(a->workspace);
+    float* dvec = dq_acc + (size_t)a->bh * a->n * 64;
+    float* lse2 = dvec + (size_t)a->bh * n_pad;
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(a->stream);
+
+    CUtensorMap mq, mk, mv, mdo;
+    int rc;
+    if ((rc = make_map(&mq, a->q, a->bh, a->n)) != BF_OK) return rc;
+    if ((rc = make_map(&mk, a->k, a->bh, a->n)) != BF_OK) return rc;
+    if ((rc = make_map(&mv, a->v, a->bh, a->n)) != BF_OK) return rc;
+    if ((rc = make_map(&mdo, a->dout, a->bh, a->n)) != BF_OK) return rc;
+    static bool done[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
+    if (!done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(bfk::bwd::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             bfk::bwd::kSmemBytesB);
+        if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
+        done[dev] = true;
+    }
+    int sms = 0;
+    if ((rc = sm_count(&sms)) != BF_OK) return rc;
+
+    cudaError_t e = cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)a->bh * a->n * 64, stream);
+    if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
+    auto launch_err = [](const char* what) -> int {
+        const cudaError_t le = cudaGetLastError();
+        if (le == cudaSuccess) return BF_OK;
+        char msg[256];
+        snprintf(msg, sizeof(msg), "%s: %s", what, cudaGetErrorString(le));
+        return bf_set_error(BF_ERR_CUDA, msg);
+    };
+    if ((rc = launch_err("before the backward")) != BF_OK) return rc;
+    bfk::bwd::bwd_prep_kernel<<<sms * 8, 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(a->o), reinterpret_cast<const __nv_bfloat16*>(a->dout), a->lse, dvec,
+        lse2, a->bh, a->n, n_pad);
+    bfk::bwd::BParams bp;
+    bp.n = a->n;
+    bp.n_pad = n_pad;
+    bp.q_tiles = (int)q_tiles;
+    bp.scale = a->scale;
+    bp.scale_log2 = a->scale * 1.4426950408889634f;
+    bp.lse2 = lse2;
+    bp.dvec = dvec;
+    bp.dq_acc = dq_acc;
+    bp.dk = reinterpret_cast<__nv_bfloat16*>(a->dk);
+    bp.dv = reinterpret_cast<__nv_bfloat16*>(a->dv);
+    bp.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
+    if ((rc = launch_err("backward prep kernel")) != BF_OK) return rc;
+    bfk::bwd::fa_bwd_kernel<<<(unsigned)blocks, bfk::bwd::kThreadsB, bfk::bwd::kSmemBytesB, stream>>>(mq, mk, mv, mdo, bp);
+    {
+        const cudaError_t le = cudaGetLastError();
+        if (le != cudaSuccess) {
+            cudaFuncAttributes fa;
+            cudaFuncGetAttributes(&fa, bfk::bwd::fa_bwd_kernel);
+            char msg[256];
+            snprintf(msg, sizeof(msg), "backward kernel: %s (regs %d, max threads %d, local %zu B, smem %d B)",
+                     cudaGetErrorString(le), fa.numRegs, fa.maxThreadsPerBlock, fa.localSizeBytes, bfk::bwd::kSmemBytesB);
+            return bf_set_error(BF_ERR_CUDA, msg);
+        }
+    }
+    bfk::bwd::bwd_dq_kernel<<<sms * 8, 256, 0, stream>>>(dq_acc, reinterpret_cast<__nv_bfloat16*>(a->dq), a->scale,
+                                                          (size_t)a->bh * a->n * 16);
+    e = cudaGetLastError();
     if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
     return BF_OK;
 }

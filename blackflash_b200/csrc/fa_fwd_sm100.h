@@ -33,4 +33,26 @@ struct BfFwdArgs {
 };
 
 int bf_fwd_launch(const BfFwdArgs* a);
+
+struct BfBwdArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    const void* o;
+    const void* dout;
+    const float* lse;  // [BH, N] natural-log logsumexp of the forward
+    void* dq;
+    void* dk;
+    void* dv;
+    void* workspace;   // bf_bwd_workspace_bytes(bh, n) bytes, 16-byte aligned
+    long long bh;
+    int n;
+    int d;
+    float scale;
+    void* stream;
+    unsigned long long timeout_ns;  // 0 = default
+};
+
+long long bf_bwd_workspace_bytes(long long bh, int n);
+int bf_bwd_launch(const BfBwdArgs* a);
 int bf_set_error(int code, const char* msg);

@@ -129,6 +129,57 @@ def attention_partial_blocks(Q: torch.Tensor, Kg: torch.Tensor, Vg: torch.Tensor
     return O, lse
 
 
+def attention_backward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, O: torch.Tensor, dO: torch.Tensor,
+                       lse: torch.Tensor, scale: float):
+    """Gradients (dQ, dK, dV) of O = softmax(scale Q K^T) V for upstream dO.
+
+    Q, K, V, O, dO: [B, H, N, 64] bf16 CUDA; lse: [B, H, N] fp32 from `forward_lse`.
+    Non-causal, d = 64. The fp32 workspace (a dQ accumulator and two row vectors)
+    is allocated here from torch's caching allocator."""
+    _check_qkv(Q, K, V)
+    for name, t in (("O", O), ("dO", dO)):
+        _require(t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.shape == Q.shape,
+                 f"{name} must be a contiguous CUDA bf16 tensor of Q's shape")
+    _require(lse.is_cuda and lse.dtype == torch.float32 and lse.is_contiguous() and lse.shape == Q.shape[:3],
+             "lse must be a contiguous CUDA fp32 [B, H, N] tensor")
+    _require(Q.size(3) == 64, "the backward supports d=64")
+    B, H, N, d = Q.shape
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(Q), torch.empty_like(Q)
+    if Q.numel() == 0:
+        return dQ, dK, dV
+    lib = _lib.load()
+    nbytes = lib.blackflash_bwd_workspace_bytes(B, H, N, d)
+    ws = torch.empty(nbytes // 4, dtype=torch.float32, device=Q.device)
+    with torch.cuda.device(Q.device):
+        rc = lib.blackflash_bwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), dO.data_ptr(), lse.data_ptr(),
+                                dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), ws.data_ptr(), nbytes, B, H, N, d,
+                                float(scale), _stream_handle(Q.device))
+    _lib.check(rc, "blackflash_bwd")
+    return dQ, dK, dV
+
+
+class _BlackFlashFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, Q, K, V, scale):
+        O, lse, _ = forward_lse(Q, K, V, scale, want_stats=True)
+        ctx.save_for_backward(Q, K, V, O, lse)
+        ctx.scale = scale
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, O, lse = ctx.saved_tensors
+        dQ, dK, dV = attention_backward(Q, K, V, O, dO.contiguous(), lse, ctx.scale)
+        return dQ, dK, dV, None
+
+
+def blackflash_with_grad(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+    """`blackflash` as a differentiable op (forward and backward on the sm_100a kernels)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(Q.size(-1))
+    return _BlackFlashFn.apply(Q, K, V, float(scale))
+
+
 def lse_merge_(O_acc: torch.Tensor, lse_acc: torch.Tensor, O_part: torch.Tensor, lse_part: torch.Tensor) -> None:
     """In-place log-sum-exp merge of a partial result into the running one (fp32)."""
     for t in (O_acc, lse_acc, O_part, lse_part):

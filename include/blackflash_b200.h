@@ -77,6 +77,21 @@ int blackflash_fwd_partial_blocks(const void* Q, const void* Kg, const void* Vg,
                                   void* stream);
 
 /*
+ * Attention backward (d = 64). No counterpart in the reference: its l / m slots
+ * (include/flash_attn.cuh:27-28) are declared for a backward pass it never built.
+ *   Q, K, V, O, dO: [B, H, N, 64] bf16 (O from the forward), lse: [B, H, N] fp32 from
+ *   blackflash_fwd's lse slot; dQ, dK, dV: [B, H, N, 64] bf16 outputs.
+ *   workspace: caller-owned device memory of at least
+ *   blackflash_bwd_workspace_bytes(B, H, N, 64) bytes (fp32 dQ accumulator and two
+ *   [B, H, N rounded up to 128] fp32 vectors); it is overwritten.
+ * Asynchronous on `stream`; three kernels and one memset.
+ */
+long long blackflash_bwd_workspace_bytes(int B, int H, int N, int d);
+int blackflash_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO, const float* lse,
+                   void* dQ, void* dK, void* dV, void* workspace, long long workspace_bytes, int B, int H, int N,
+                   int d, float scale, void* stream);
+
+/*
  * Log-sum-exp merge of one partial result into a running one, in place:
  *   lse' = log(exp(lse_acc) + exp(lse_part))
  *   O'   = O_acc * exp(lse_acc - lse') + O_part * exp(lse_part - lse')

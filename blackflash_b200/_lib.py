@@ -23,6 +23,7 @@ EXPORTED = (
     "blackflash_f32_to_bf16",
     "blackflash_bwd",
     "blackflash_bwd_workspace_bytes",
+    "blackflash_bwd_noalloc",
     "blackflash_status",
     "blackflash_fwd_timeout_probe",
     "blackflash_fwd_debug_s",
@@ -44,6 +45,7 @@ _SIGS = {
     "blackflash_lse_merge": (_i, [_vp, _vp, _vp, _vp, _ll, _i, _vp]),
     "blackflash_bwd": (_i, [_vp] * 10 + [_ll, _i, _i, _i, _i, _f, _vp]),
     "blackflash_bwd_workspace_bytes": (_ll, [_i, _i, _i, _i]),
+    "blackflash_bwd_noalloc": (_i, [_vp] * 9 + [_i, _i, _i, _i, _f, _vp]),
     "blackflash_f32_to_bf16": (_i, [_vp, _vp, _ll, _vp]),
     "blackflash_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
     "blackflash_fwd_timeout_probe": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, ctypes.c_ulonglong, _vp]),

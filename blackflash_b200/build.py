@@ -18,7 +18,7 @@ LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libblackflash_b200.so")
 HARNESS_PATH = os.path.join(LIB_DIR, "flash_attn")
 
-SOURCES = ["fa_fwd_sm100.cu", "capi.cu", "lse_merge.cu"]
+SOURCES = ["fa_fwd_sm100.cu", "capi.cu", "lse_merge.cu", "noalloc.cu"]
 HEADERS = ["sm100_ptx.cuh", "fa_fwd_sm100.h", "fa_fwd_sm100_d128.cuh", "fa_bwd_sm100.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", os.path.join(REPO_DIR, "include")]

@@ -92,6 +92,22 @@ int blackflash_bwd(const void* Q, const void* K, const void* V, const void* O, c
                    int d, float scale, void* stream);
 
 /*
+ * The backward without a workspace argument, for callers that cannot allocate
+ * device memory: plugins whose host owns the whole device pool, or loops that
+ * cannot afford the synchronisation cudaMalloc / cudaFree may bring. No
+ * counterpart in the reference. It allocates nothing; its scratch is a fixed
+ * 64 MiB array inside the library on every device that loads it, so
+ * B * H * N is limited to about 250000 rows (larger problems get BF_ERR_ARG and
+ * belong to blackflash_bwd). The first call on a device looks up the array's
+ * device address; make it before any stream capture. All calls on a device share
+ * the array: calls in order on one stream are fine, calls that overlap on the
+ * GPU race. Arguments as blackflash_bwd.
+ */
+int blackflash_bwd_noalloc(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                           const float* lse, void* dQ, void* dK, void* dV, int B, int H, int N, int d, float scale,
+                           void* stream);
+
+/*
  * Log-sum-exp merge of one partial result into a running one, in place:
  *   lse' = log(exp(lse_acc) + exp(lse_part))
  *   O'   = O_acc * exp(lse_acc - lse') + O_part * exp(lse_part - lse')

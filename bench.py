@@ -49,6 +49,9 @@ CONFIGS = {
     "prof": (16, 64, 1024, 64, "normal"),
     # head dimension 128 (extension; the reference kernel is d = 64 only)
     "d128": (16, 16, 4096, 128, "normal"),
+    # attention backward (extension), d = 64: a main case and a small profiling case
+    "bwd": (16, 16, 4096, 64, "normal"),
+    "bwdprof": (4, 16, 2048, 64, "normal"),
 }
 METRIC = "attention fwd TFLOPS (4BHN^2d/t)"
 
@@ -189,6 +192,61 @@ def run_reference(args, cfg_name):
                    "parallelism": "cpu host cores (rank 0 only)"},
         "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_bwd(args, cfg_name):
+    """Backward configs (one GPU): `attention_backward` on inputs resident in HBM, after one
+    forward for O and lse (outside the timed region). FLOPs are counted as 2.5x the forward's."""
+    from blackflash_b200 import attention_backward, forward_lse
+    from blackflash_b200.inputs import make_qkv
+
+    world, rank, local = dist_env()
+    if world != 1:
+        raise SystemExit("backward configs run on one GPU")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, H, N, d, dist = CONFIGS[cfg_name]
+    q, k, v = make_qkv(B, H, N, d, dist=dist, seed=1000, device=dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    do = torch.randn(q.shape, generator=g, device=dev).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(d)
+    O, lse, _ = forward_lse(q, k, v, scale)
+    for _ in range(args.warmup):
+        attention_backward(q, k, v, O, do, lse, scale)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        attention_backward(q, k, v, O, do, lse, scale)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    h1 = time.time()
+    sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    f = 2.5 * flops(B, H, N, d)
+    value = f / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+    line = {
+        "metric": "attention bwd TFLOPS (2.5*4BHN^2d/t)", "value": value, "unit": "TFLOPS", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"backward B={B} H={H} N={N} d={d} {dist}, non-causal, scale 1/sqrt({d})",
+                   "global_batch": B, "seq_len": N, "parallelism": "single GPU",
+                   "l2": "inputs larger than L2" if 5 * q.numel() * 2 > 126e6 else "inputs fit in L2"},
+        "roofline": {"bound": "tensor", "achieved": value, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": value / peaks["bf16_tflops"], "traffic": None,
+                     "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
+                     "kernel": "fa_bwd_kernel (+ bwd_prep_kernel, bwd_dq_kernel, dq memset)"},
+        "cpu_baseline": None,
+        "clocks": sampler.summary(h0, h1),
+        "gpu_launches": args.steps * 3,
     }
     print(json.dumps(line), flush=True)
 
@@ -479,6 +537,8 @@ def main():
         run_reference(args, args.config)
     elif args.config == "5":
         run_ring(args, args.config)
+    elif args.config in ("bwd", "bwdprof"):
+        run_bwd(args, args.config)
     else:
         run_ours(args, args.config)
 

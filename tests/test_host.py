@@ -66,6 +66,27 @@ def test_argument_errors_without_device_work():
     assert lib.blackflash_f32_to_bf16(16, 16, 0, None) == _lib.BF_OK
 
 
+def test_backward_argument_errors_without_device_work():
+    """The backward entry points reject bad arguments before any CUDA call."""
+    from blackflash_b200 import _lib
+    lib = _lib.load()
+    assert lib.blackflash_bwd_workspace_bytes(1, 1, 128, 64) == 4 * (128 * 64 + 2 * 128)
+    assert lib.blackflash_bwd_workspace_bytes(1, 1, 100, 64) == 4 * (100 * 64 + 2 * 128)  # vectors padded to 128
+    assert lib.blackflash_bwd_workspace_bytes(1, 1, 128, 128) == 0  # d = 64 only
+    ptrs = [16] * 10
+    rc = lib.blackflash_bwd(*ptrs, 1 << 20, 1, 1, 128, 128, 0.125, None)
+    assert rc == _lib.BF_ERR_ARG and b"d=64" in lib.blackflash_last_error()
+    rc = lib.blackflash_bwd(*ptrs, 16, 1, 1, 128, 64, 0.125, None)
+    assert rc == _lib.BF_ERR_ARG and b"workspace" in lib.blackflash_last_error()
+    rc = lib.blackflash_bwd(*ptrs, 1 << 20, 0, 1, 128, 64, 0.125, None)
+    assert rc == _lib.BF_ERR_ARG
+    # no-workspace variant: problems beyond its fixed scratch are refused up front
+    rc = lib.blackflash_bwd_noalloc(*ptrs[:9], 64, 64, 1024, 64, 0.125, None)
+    assert rc == _lib.BF_ERR_ARG and b"64 MiB" in lib.blackflash_last_error()
+    rc = lib.blackflash_bwd_noalloc(*ptrs[:9], 1, 1, 128, 128, 0.125, None)
+    assert rc == _lib.BF_ERR_ARG and b"d=64" in lib.blackflash_last_error()
+
+
 def test_python_checks_mirror_the_reference_binding():
     """Same failures as binding/blackflash_ops.cu:24-34: RuntimeError on CPU / non-bf16 / non-contiguous / d != 64."""
     from blackflash_b200 import blackflash, forward

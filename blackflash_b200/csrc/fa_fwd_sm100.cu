@@ -6,7 +6,7 @@
 // fp32 accumulation. The reference's row-max / logsumexp slots
 // (include/flash_attn.cuh:27-28, never written there) are filled here.
 //
-// Persistent kernel: one CTA per SM (608 threads) walks work items
+// Persistent kernel: one CTA per SM (640 threads; 608 without BF_REGSPLIT) walks work items
 // item = blockIdx.x + k * gridDim.x; an item is two 128-row query tiles
 // (256 rows) of one (b, h) slice against all of its KV rows. Roles:
 //   * warps 0-7 / 8-15: softmax for query tile 0 / 1, four warps per

@@ -208,3 +208,15 @@ def test_allgather_schedule_on_gloo_matches_full_attention(world, tmp_path):
     o_ref, lse_ref, _ = oracle.attn_exact(q, k, v, 0.125)
     np.testing.assert_allclose(o, o_ref, atol=2e-5)
     np.testing.assert_allclose(lse, lse_ref, atol=2e-4)
+
+
+def test_build_tracks_every_source_and_header():
+    """A file in csrc/ missing from the build's lists would leave a stale library after an
+    edit (the rebuild check compares modification times of the listed files only)."""
+    import glob
+
+    from blackflash_b200 import build
+    listed = set(build.SOURCES) | set(build.HEADERS) | {"harness.cu"}
+    present = {os.path.basename(f) for f in glob.glob(os.path.join(build.CSRC, "*"))
+               if f.endswith((".cu", ".cuh", ".h"))}
+    assert present <= listed, sorted(present - listed)

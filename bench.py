@@ -168,29 +168,64 @@ def cpu_reference_sample(B, H, N, d, dist, budget_s: float, seed: int = 0):
     return 4.0 * done * rows * N * d / el / 1e12, sample, el, torch.get_num_threads()
 
 
+def workload_desc(B, H, N, d, dist):
+    """The workload string both arms print (the same for the same configuration)."""
+    return f"B={B} H={H} N={N} d={d} {dist}, non-causal, scale 1/sqrt({d})"
+
+
+# Reference-arm steps run the whole workload when it takes at most this many seconds
+# on the host (config 3: ~3 s on 16 cores); larger configs time a bounded sample.
+REF_FULL_MAX_FLOP = 4.0 * 64 * 64 * 1024 * 1024 * 64
+
+
 def run_reference(args, cfg_name):
+    """The reference's CPU path (torch fp32 math, tests/test_blackflash.py:16-19) on all
+    host threads, rank 0 only. For configs up to config 3's size every step computes the
+    whole workload (every (b,h) slice), so ms_per_step is a measured step time; larger
+    configs time a bounded sample of slices per step and say so."""
     world, rank, _ = dist_env()
     if rank != 0:
         return  # rank 0 alone runs the CPU reference
+    from blackflash_b200.inputs import make_qkv
+    from oracle import oracle
     B, H, N, d, dist = CONFIGS[cfg_name]
-    per_step = []
-    for _ in range(args.warmup):
-        cpu_reference_sample(B, H, N, d, dist, budget_s=0.5)
-    desc = ""
-    threads = 1
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    scale = 1.0 / math.sqrt(d)
+    full = flops(B, H, N, d) <= REF_FULL_MAX_FLOP
+    if full:
+        q, k, v = (t.reshape(B * H, N, d) for t in make_qkv(B, H, N, d, dist=dist, seed=1000))
+        chunk = 4
+
+        def step():
+            for s0 in range(0, B * H, chunk):
+                oracle.torch_math(q[s0:s0 + chunk], k[s0:s0 + chunk], v[s0:s0 + chunk], scale)
+            return flops(B, H, N, d)
+        sample = f"whole workload every step: all {B*H} (b,h) slices, torch fp32 CPU math, {chunk} slices per call"
+    else:
+        budget = args.ref_step_seconds
+
+        def step():
+            tf, _, el, _ = cpu_reference_sample(B, H, N, d, dist, budget_s=budget)
+            return tf * 1e12 * el
+        sample = (f"bounded sample per step (about {budget:.0f} s of whole slices, at most 2048 query rows each); "
+                  f"TFLOPS = sampled FLOPs / time")
+    for _ in range(args.warmup if full else 1):
+        step()
+    t_total, f_total = 0.0, 0.0
     for _ in range(args.steps):
-        tf, desc, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.ref_step_seconds)
-        per_step.append(tf)
-    value = statistics.mean(per_step)
-    sample = f"{desc} per step, N={N}, torch fp32 CPU math; TFLOPS = 4*rows*N*d per sampled slice / time"
+        t0 = time.perf_counter()
+        f_total += step()
+        t_total += time.perf_counter() - t0
+    value = f_total / t_total / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": flops(B, H, N, d) / (value * 1e12) * 1e3 if value > 0 else None,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_total / args.steps * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal", "global_batch": B, "seq_len": N,
+        "config": {"workload": workload_desc(B, H, N, d, dist), "global_batch": B, "seq_len": N,
                    "parallelism": "cpu host cores (rank 0 only)"},
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -249,6 +284,31 @@ def run_bwd(args, cfg_name):
         "gpu_launches": args.steps * 3,
     }
     print(json.dumps(line), flush=True)
+
+
+def cudnn_comparator(q, k, v, scale, f_launch, steps=10):
+    """The vendor library on the same device and the same inputs: torch SDPA restricted to
+    its cuDNN backend, timed with CUDA events after the main timed region (not part of
+    `value`). Returns TFLOPS, or the reason it could not run."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from torch.nn.functional import scaled_dot_product_attention as sdpa
+    try:
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            for _ in range(3):
+                out = sdpa(q, k, v, scale=scale)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                out = sdpa(q, k, v, scale=scale)
+            e1.record()
+            torch.cuda.synchronize()
+        del out
+    except RuntimeError as e:
+        return {"unavailable": str(e).splitlines()[0][:200]}
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": f_launch / (ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_launch": ms,
+            "what": "torch SDPA, cuDNN backend only, same inputs and device, CUDA events"}
 
 
 def run_ours(args, cfg_name):
@@ -349,6 +409,10 @@ def run_ours(args, cfg_name):
     bytes_in = 3 * q.numel() * q.element_size()
     bytes_out = O.numel() * O.element_size()
 
+    comparators = None
+    if world == 1 and not args.no_comparators:
+        comparators = {"cudnn_sdpa": cudnn_comparator(q, k, v, scale, f_rank)}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, desc, el, threads = cpu_reference_sample(B, H, N, d, dist, budget_s=args.cpu_seconds)
@@ -361,11 +425,13 @@ def run_ours(args, cfg_name):
         per_gpu_achieved = f_rank / (ms_local / args.steps * 1e-3) / 1e12  # rank 0's kernel rate
         peak = peaks["bf16_tflops"]
         traffic = TRAFFIC_BYTES.get(cfg_name)
+        if traffic is not None:
+            traffic *= my / total  # per launch on this rank: traffic is linear in the slice count
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"B={B} H={H} N={N} d={d} {dist}, non-causal, scale 1/sqrt({d})",
+            "config": {"workload": workload_desc(B, H, N, d, dist),
                        "global_batch": B, "seq_len": N, "parallelism": f"bxh{world} (no collective)",
                        "l2": "inputs larger than L2 (no flush)", "slices_per_rank": my},
             "roofline": {"bound": "tensor", "achieved": per_gpu_achieved, "peak": peak, "unit": "TFLOP/s",
@@ -378,6 +444,8 @@ def run_ours(args, cfg_name):
                     "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms},
             "gpu_launches": args.steps,
         }
+        if comparators is not None:
+            line["comparators"] = comparators
         print(json.dumps(line), flush=True)
     if world > 1:
         dist_mod.destroy_process_group()
@@ -528,6 +596,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-comparators", action="store_true", help="skip the cuDNN SDPA comparison")
     ap.add_argument("--sp-mode", choices=["ring", "ring1", "allgather"], default="ring",
                     help="sequence-parallel schedule of config 5")
     args = ap.parse_args()

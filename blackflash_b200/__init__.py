@@ -8,7 +8,5 @@ is no CPU fallback.
 """
 from .ops import (attention_backward, attention_partial, attention_partial_blocks, blackflash, blackflash_with_grad, blackflash_host, forward, forward_lse,  # noqa: F401
                   lse_merge_, to_bf16, wait_status)
-from . import blackflash_cuda  # noqa: F401
 
-__all__ = ["blackflash", "blackflash_with_grad", "attention_backward", "blackflash_host", "forward", "forward_lse", "attention_partial", "attention_partial_blocks", "lse_merge_", "to_bf16", "wait_status",
-           "blackflash_cuda"]
+__all__ = ["blackflash", "blackflash_with_grad", "attention_backward", "blackflash_host", "forward", "forward_lse", "attention_partial", "attention_partial_blocks", "lse_merge_", "to_bf16", "wait_status"]

@@ -1,4 +1,5 @@
-// C-ABI entry points (include/blackflash_b200.h) and the C++ launcher with the
+// C-ABI entry points (include/blackflash_b200.h, test hooks in
+// include/blackflash_b200_diag.h) and the C++ launcher with the
 // reference's signature (include/flash_attn.cuh). All argument checking that
 // does not need the device lives in bf_fwd_launch (fa_fwd_sm100.cu).
 #include <stdio.h>

@@ -6,7 +6,7 @@
 // fp32 accumulation. The reference's row-max / logsumexp slots
 // (include/flash_attn.cuh:27-28, never written there) are filled here.
 //
-// Persistent kernel: one CTA per SM (640 threads; 608 without BF_REGSPLIT) walks work items
+// Persistent kernel: one CTA per SM (640 threads) walks work items
 // item = blockIdx.x + k * gridDim.x; an item is two 128-row query tiles
 // (256 rows) of one (b, h) slice against all of its KV rows. Roles:
 //   * warps 0-7 / 8-15: softmax for query tile 0 / 1, four warps per
@@ -46,6 +46,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+
 namespace bfk {
 
 // Set by a bounded wait that gave up; read by blackflash_status().
@@ -64,38 +66,15 @@ constexpr int kSoftWarps = 16;                       // 8 per query tile, 4 per 
 // warpgroup) so setmaxnreg can move registers from the issuer warps to the softmax.
 constexpr int kThreads = kSoftWarps * 32 + (BF_REGSPLIT ? 4 : 3) * 32;  // + TMA producer, S issuer, PV issuer
 constexpr int kTileBytes = kBM * kD * 2;  // 16 KiB (Q, K, V or O tile, bf16)
-// BF_MMA_ROWSUM: the row sum l comes from the tensor core (an N=16 MMA of P against an
-// all-ones tile into TMEM after each PV) instead of FADDs in the softmax. The two tiles
-// then share one P buffer in TMEM to make room for the sum columns.
-#ifndef BF_MMA_ROWSUM
-#define BF_MMA_ROWSUM 0
-#endif
-constexpr bool kMmaRowSum = BF_MMA_ROWSUM != 0;
 constexpr int kTmemCols = 512;
-// TMEM columns: S_t at t*128; P_t (bf16, 64 columns) and O_t (fp32, 64 columns) after
-// them. With kMmaRowSum one P buffer serves both tiles and L_t (16 columns) follows O.
+// TMEM columns: S_t at t*128; P_t (bf16, 64 columns) and O_t (fp32, 64 columns) after them.
 constexpr int kColS = 0;
 constexpr int kColP = 2 * 128;
-constexpr int kColO = kColP + (BF_MMA_ROWSUM ? 1 : 2) * 64;
-constexpr int kColL = kColO + 2 * 64;
-static_assert(kColL + (BF_MMA_ROWSUM ? 32 : 0) <= kTmemCols, "TMEM columns");
+constexpr int kColO = kColP + 2 * 64;
+static_assert(kColO + 2 * 64 <= kTmemCols, "TMEM columns");
 constexpr int kProducerWarp = 16;  // TMA producer
 constexpr int kSWarp = 17;         // issues S = Q K^T; owns the TMEM allocation
 constexpr int kPVWarp = 18;        // issues O += P V
-#ifdef BF_PERF_DECOUPLE
-constexpr bool kPerfDecouple = true;  // perf experiment only: MMA and softmax do not wait on each other
-#else
-constexpr bool kPerfDecouple = false;
-#endif
-#ifndef BF_LAZY_MAX
-#define BF_LAZY_MAX 0
-#endif
-constexpr bool kLazyMax = BF_LAZY_MAX != 0;
-#ifndef BF_DEFER_P
-#define BF_DEFER_P 0
-#endif
-static_assert(!(BF_MMA_ROWSUM && (BF_DEFER_P || BF_LAZY_MAX)), "BF_MMA_ROWSUM excludes BF_DEFER_P and BF_LAZY_MAX");
-
 #ifndef BF_EMU_PAIRS
 #define BF_EMU_PAIRS 1
 #endif
@@ -111,8 +90,7 @@ constexpr int kOffQ = 0;                                  // [2 buffers][2 tiles
 constexpr int kOffK = kOffQ + 2 * kQTiles * kTileBytes;   // [kStages]
 constexpr int kOffV = kOffK + kStages * kTileBytes;       // [kStages]
 constexpr int kOffO = kOffV + kStages * kTileBytes;       // [2 tiles] bf16 output staging
-constexpr int kOffOnes = kOffO + kQTiles * kTileBytes;    // 2 KiB of bf16 1.0 (kMmaRowSum)
-constexpr int kOffBar = kOffOnes + (BF_MMA_ROWSUM ? 2048 : 0);
+constexpr int kOffBar = kOffO + kQTiles * kTileBytes;
 
 struct Bars {
     uint64_t q_full[2];
@@ -251,14 +229,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         bars->abort_flag = 0;
         fence_barrier_init();
     }
-    if constexpr (kMmaRowSum) {
-        // bf16 1.0 everywhere: whatever element order the descriptor walks, B is all ones.
-        if (warp >= kSoftWarps) {
-            uint32_t* ones = reinterpret_cast<uint32_t*>(smem + kOffOnes);
-            for (int i = threadIdx.x - kSoftWarps * 32; i < 512; i += kThreads - kSoftWarps * 32) ones[i] = 0x3F803F80u;
-            fence_proxy_async_smem();
-        }
-    }
     if (warp == kProducerWarp && lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -296,28 +266,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = quarter * 32 + sub * 16 + (lane & 15);  // row within the tile == TMEM lane
         const uint32_t lane_off = (uint32_t)(quarter * 32 + sub * 16) << 16;
         const uint32_t tS = tmem + lane_off + (uint32_t)(kColS + t * kBN);
-        const uint32_t tP = tmem + lane_off + (uint32_t)(kColP + (kMmaRowSum ? 0 : t * kD));
+        const uint32_t tP = tmem + lane_off + (uint32_t)(kColP + t * kD);
         const uint32_t tO = tmem + lane_off + (uint32_t)(kColO + t * kD);
-        const uint32_t tL = tmem + lane_off + (uint32_t)(kColL + t * 16);  // kMmaRowSum only
         const float sl2 = p.scale_log2;
         const uint64_t sl2_2 = f2_pack(sl2, sl2);
         const uint32_t bar_s = smem_addr(&bars->s_full[t]);
         const uint32_t bar_se = smem_addr(&bars->s_empty[t]);
         const uint32_t bar_p = smem_addr(&bars->p_full[t]);
         const uint32_t bar_pv = smem_addr(&bars->pv_done[t]);
-        // The PV that reads P last before this tile rewrites it: its own previous one, or
-        // with the shared P buffer the other tile's (tile 0 waits PV_1(g-1), tile 1 PV_0(g)).
-        // Commits cover all earlier MMAs of the issuing thread, so either wait also
-        // guarantees this tile's own PV(g-1) (O and L final before a rescale).
-        const uint32_t bar_preuse = smem_addr(&bars->pv_done[kMmaRowSum ? 1 - t : t]);
+        // P_t is rewritten only after PV_t of the previous step has read it.
+        const uint32_t bar_preuse = bar_pv;
         const bool issuer = (warp & 7) == 0 && lane == 0;  // issues tile t's TMA stores
         const bool tracing = trace_hit && issuer;
         uint8_t* stage = smem + kOffO + t * kTileBytes;
         uint32_t g = 0;  // global KV step of this CTA
         bool ok = true;
-#if BF_DEFER_P
-        bool p_pending = false;  // P stored but p_full not yet signalled
-#endif
 
         for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
             int bh, q_row0;
@@ -329,22 +292,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             for (int j = 0; j < nk_item; ++j, ++g) {
                 BF_TRACE(t, g, 0);
-                if (!kPerfDecouple && !(ok = warp_wait(bar_s, g & 1u, ctl, kSiteSoftS))) break;
+                if (!(ok = warp_wait(bar_s, g & 1u, ctl, kSiteSoftS))) break;
                 tc_fence_after();
                 BF_TRACE(t, g, 1);
 
                 uint32_t s[2][32];  // columns 64h + [0, 32) and 64h + [32, 64)
                 tmem_ld16x32bx2_x32<64>(tS + 0, s[0]);
                 tmem_ld16x32bx2_x32<64>(tS + 32, s[1]);
-#if BF_DEFER_P
-                if (p_pending) {
-                    // P of the previous step: its store latency overlaps this step's S load.
-                    tmem_wait_st();
-                    tc_fence_before();
-                    mbar_arrive(bar_p);
-                    p_pending = false;
-                }
-#endif
                 tmem_wait_ld();
                 BF_TRACE(t, g, 2);
 
@@ -378,24 +332,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint64_t x2 = f2_fma(
                                 f2_pack(__uint_as_float(s[q][2 * c]), __uint_as_float(s[q][2 * c + 1])), sl2_2, negm_2);
                             uint64_t p2;
-#ifdef BF_PERF_NO_EXP
-                            if (true) {
-                                p2 = x2;  // perf experiment only: exponentials skipped, results are wrong
-                            } else
-#endif
                             if (((q * 16 + c) & (kEmuPeriod - 1)) < kEmuPairs) {
-                                p2 = exp2_poly_x2<kLazyMax>(x2);
+                                p2 = exp2_poly_x2(x2);
                             } else {
                                 float x0, x1;
                                 f2_unpack(x2, x0, x1);
                                 p2 = f2_pack(fast_exp2(x0), fast_exp2(x1));
                             }
-                            if constexpr (!kMmaRowSum) {
-                                if (c & 1)
-                                    sum_b = f2_add(sum_b, p2);
-                                else
-                                    sum_a = f2_add(sum_a, p2);
-                            }
+                            if (c & 1)
+                                sum_b = f2_add(sum_b, p2);
+                            else
+                                sum_a = f2_add(sum_a, p2);
                             float p0, p1;
                             f2_unpack(p2, p0, p1);
                             pk[q][c] = pack_bf16x2(p0, p1);
@@ -417,71 +364,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));  // the row's other half
                 };
 
-                bool need;
+                tc_fence_before();
+                mbar_arrive(bar_se);  // S_t is in registers: it may now be overwritten
+                const float mx = row_max();
+                m_raw = fmaxf(m_raw, mx);
+                const float m_new = mx * sl2;
+                BF_TRACE(t, g, 3);
+                // Lazy rescale: keep the old reference max unless the tile max exceeds
+                // it by more than 8 (log2 units), i.e. P entries stay <= 256.
+                const bool need = m_new > m_use + 8.0f;
                 float alpha = 1.f;
-                if constexpr (!kLazyMax) {
-                    tc_fence_before();
-                    mbar_arrive(bar_se);  // S_t is in registers: it may now be overwritten
-                    const float mx = row_max();
-                    m_raw = fmaxf(m_raw, mx);
-                    const float m_new = mx * sl2;
-                    BF_TRACE(t, g, 3);
-                    // Lazy rescale: keep the old reference max unless the tile max exceeds
-                    // it by more than 8 (log2 units), i.e. P entries stay <= 256.
-                    need = m_new > m_use + 8.0f;
-                    if (need) {
-                        alpha = fast_exp2(m_use - m_new);  // 0 on the first tile
-                        m_use = m_new;
-                    }
-                    if constexpr (kMmaRowSum)
-                        exps(m_use);
-                    else
-                        l_half = l_half * alpha + exps(m_use);
-                } else {
-                    // The tile max is computed only on a slice's first tile (or when row_max
-                    // is requested). Later tiles use the reference max directly and check the
-                    // row sum: it exceeds 2^16 (or is inf) exactly when some entry got large.
-                    // Then the max is taken from S (still in TMEM: s_empty is signalled only
-                    // after this check) and the tile is recomputed.
-                    if (j == 0 || p.row_max != nullptr) {
-                        const float mx = row_max();
-                        m_raw = fmaxf(m_raw, mx);
-                        if (j == 0) m_use = mx * sl2;
-                    }
-                    BF_TRACE(t, g, 3);
-                    float part = exps(m_use);
-                    const float tot = part + __shfl_xor_sync(0xffffffffu, part, 16);
-                    need = !(tot <= 65536.f);
-                    if (__any_sync(0xffffffffu, need)) {
-                        tmem_ld16x32bx2_x32<64>(tS + 0, s[0]);
-                        tmem_ld16x32bx2_x32<64>(tS + 32, s[1]);
-                        tmem_wait_ld();
-                        if (valid < 64) {
-#pragma unroll
-                            for (int c = 0; c < 64; ++c)
-                                if (c >= valid) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
-                        }
-                        const float mx = row_max();
-                        m_raw = fmaxf(m_raw, mx);
-                        if (need) {
-                            const float m_new = mx * sl2;
-                            alpha = fast_exp2(m_use - m_new);
-                            m_use = m_new;
-                        }
-                        part = exps(m_use);
-                    }
-                    l_half = l_half * alpha + part;
-                    tc_fence_before();
-                    mbar_arrive(bar_se);  // no more reads of S_t
+                if (need) {
+                    alpha = fast_exp2(m_use - m_new);  // 0 on the first tile
+                    m_use = m_new;
                 }
+                l_half = l_half * alpha + exps(m_use);
                 BF_TRACE(t, g, 4);
 
                 // P_t of the previous step must have been consumed (and O_t be final)
                 // before we overwrite P_t / rescale O_t.
-                if (kMmaRowSum && t == 1 && !kPerfDecouple) {
-                    if (!(ok = warp_wait(bar_preuse, g & 1u, ctl, kSiteSoftPV))) break;
-                    tc_fence_after();
-                } else if (g > 0 && !kPerfDecouple) {
+                if (g > 0) {
                     if (!(ok = warp_wait(bar_preuse, (g - 1) & 1u, ctl, kSiteSoftPV))) break;
                     tc_fence_after();
                 }
@@ -493,47 +395,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
                     tmem_st16x32bx2_x32<32>(tO, o);
-                    if constexpr (kMmaRowSum) {
-                        const uint32_t lv = tmem_ld16x32bx2_x1<8>(tL);
-                        tmem_wait_ld();
-                        tmem_st16x32bx2_x1<8>(tL, __float_as_uint(__uint_as_float(lv) * alpha));
-                    }
                 }
                 // bf16 P: this thread's 64 S columns are P columns 32h + [0, 32).
                 tmem_st16x32bx2_x16<32>(tP, pk[0]);
                 tmem_st16x32bx2_x16<32>(tP + 16, pk[1]);
-#if BF_DEFER_P
-                p_pending = true;  // completed and signalled early in the next step
-#else
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(bar_p);
-#endif
                 BF_TRACE(t, g, 6);
             }
-#if BF_DEFER_P
-            if (p_pending) {
-                tmem_wait_st();
-                tc_fence_before();
-                mbar_arrive(bar_p);
-                p_pending = false;
-            }
-#endif
             if (!ok) break;
 
             // ---------------------------------------------------- epilogue of this item
-            if (!kPerfDecouple && !(ok = warp_wait(bar_pv, (g - 1) & 1u, ctl, kSiteSoftO))) break;
+            if (!(ok = warp_wait(bar_pv, (g - 1) & 1u, ctl, kSiteSoftO))) break;
             tc_fence_after();
             uint32_t o[32];
             tmem_ld16x32bx2_x32<32>(tO, o);
-            float l_sum;
-            if constexpr (kMmaRowSum) {
-                l_sum = __uint_as_float(tmem_ld16x32bx2_x1<8>(tL));  // every L column holds the row sum
-                tmem_wait_ld();
-            } else {
-                tmem_wait_ld();
-                l_sum = l_half + __shfl_xor_sync(0xffffffffu, l_half, 16);
-            }
+            tmem_wait_ld();
+            const float l_sum = l_half + __shfl_xor_sync(0xffffffffu, l_half, 16);
             const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
             const int q_row = q_row0 + t * kBM + row;
             const bool row_ok = q_row < p.n_q;
@@ -652,7 +531,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // busy softmax warps, and the tensor core's issue queue is shallow.
         constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);  // Q (K-major) x K (K-major)
         constexpr uint32_t kIdescO = idesc_bf16_f32(kBM, kD, 1);   // P (TMEM)   x V (MN-major)
-        constexpr uint32_t kIdescL = idesc_bf16_f32(kBM, 16, 1);   // P (TMEM)   x ones (N = 16)
         const bool leader = elect_one();
         const bool tracing = trace_hit && leader;
         const uint64_t desc_base = smem_desc_sw128(smem_addr(smem), 16, 1024);
@@ -660,7 +538,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t desc_lo0 = (uint32_t)desc_base;  // low word of a descriptor at smem offset 0
         constexpr uint32_t kTileLo = kTileBytes >> 4;   // low-word step between 16 KiB tiles
         const uint32_t q_lo0 = desc_lo0 + (kOffQ >> 4), k_lo0 = desc_lo0 + (kOffK >> 4), v_lo0 = desc_lo0 + (kOffV >> 4);
-        const uint32_t ones_lo = desc_lo0 + (kOffOnes >> 4);
         const uint32_t q_full0 = smem_addr(&bars->q_full[0]), q_empty0 = smem_addr(&bars->q_empty[0]);
         const uint32_t k_full0 = smem_addr(&bars->k_full[0]), k_empty0 = smem_addr(&bars->k_empty[0]);
         const uint32_t v_full0 = smem_addr(&bars->v_full[0]), v_empty0 = smem_addr(&bars->v_empty[0]);
@@ -692,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t k_lo = k_lo0 + (uint32_t)st * kTileLo;
 #pragma unroll
                     for (int t = 0; t < kQTiles; ++t) {
-                        if (g > 0 && !kPerfDecouple) {
+                        if (g > 0) {
                             if (!(ok = warp_wait(s_empty0 + 8 * t, (g - 1) & 1u, ctl, kSiteMmaK + 1 + t))) break;
                             tc_fence_after();
                         }
@@ -720,22 +597,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t v_lo = v_lo0 + (uint32_t)st * kTileLo;
 #pragma unroll
                     for (int t = 0; t < kQTiles; ++t) {
-                        if (!kPerfDecouple && !(ok = warp_wait(p_full0 + 8 * t, g & 1u, ctl, kSiteMmaV + 1 + t))) break;
+                        if (!(ok = warp_wait(p_full0 + 8 * t, g & 1u, ctl, kSiteMmaV + 1 + t))) break;
                         tc_fence_after();
                         BF_TRACE(2, g, 6 + t);  // PV_t(g) issue starts
                         if (leader) {
-                            const uint32_t p_col = tmem + kColP + (kMmaRowSum ? 0 : t * kD);
+                            const uint32_t p_col = tmem + kColP + t * kD;
 #pragma unroll
                             for (int kk = 0; kk < kBN / 16; ++kk)  // 16 KV rows: 8 TMEM columns of P, 16 x 128 B of V
                                 umma_ts_lo(tmem + kColO + t * kD, p_col + kk * 8, v_lo + kk * 128, desc_hi, kIdescO,
                                            (j > 0 || kk > 0) ? 1u : 0u);
-                            if constexpr (kMmaRowSum) {
-                                // L_t += P 1: every K step reads the same 2 KiB of ones.
-#pragma unroll
-                                for (int kk = 0; kk < kBN / 16; ++kk)
-                                    umma_ts_lo(tmem + kColL + t * 16, p_col + kk * 8, ones_lo, desc_hi, kIdescL,
-                                               (j > 0 || kk > 0) ? 1u : 0u);
-                            }
                             umma_commit(pv_done0 + 8 * t);
                         }
                         __syncwarp();
@@ -823,7 +693,7 @@ int make_map(CUtensorMap* m, const void* base, long long bh, int rows, int d = b
 
 template <bool kF32Out>
 int configure_once() {
-    static bool done[64] = {false};
+    static std::atomic<bool> done[64];  // per device; zero-initialised (static storage)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
     if (!done[dev]) {
@@ -838,7 +708,7 @@ int configure_once() {
 }  // namespace
 
 int sm_count(int* out) {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
     if (!cached[dev]) {
@@ -889,7 +759,7 @@ int bf_fwd_launch(const BfFwdArgs* a) {
         kp.causal = a->causal;
         kp.kv_skip = -1;
         kp.bh_count = (int)a->bh;
-        static bool done[64] = {false};
+        static std::atomic<bool> done[64];  // per device; zero-initialised (static storage)
         int dev = 0;
         if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
         if (!done[dev]) {
@@ -950,7 +820,7 @@ int bf_fwd_launch(const BfFwdArgs* a) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(a->stream);
     if (a->trace) {
         if (a->o_f32) return bf_set_error(BF_ERR_ARG, "trace runs use the bf16 output");
-        static bool traced_cfg[64] = {false};
+        static std::atomic<bool> traced_cfg[64];
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev >= 0 && dev < 64 && !traced_cfg[dev]) {
@@ -999,7 +869,7 @@ int bf_bwd_launch(const BfBwdArgs* a) {
     if ((rc = make_map(&mk, a->k, a->bh, a->n)) != BF_OK) return rc;
     if ((rc = make_map(&mv, a->v, a->bh, a->n)) != BF_OK) return rc;
     if ((rc = make_map(&mdo, a->dout, a->bh, a->n)) != BF_OK) return rc;
-    static bool done[64] = {false};
+    static std::atomic<bool> done[64];  // per device; zero-initialised (static storage)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
     if (!done[dev]) {

@@ -2,7 +2,7 @@
 #pragma once
 #include <stdint.h>
 
-#include "../../include/blackflash_b200.h"
+#include "../../include/blackflash_b200_diag.h"
 
 struct BfFwdArgs {
     const void* q;

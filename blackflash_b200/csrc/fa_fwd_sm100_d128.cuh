@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             f2_fma(f2_pack(__uint_as_float(s[q][2 * c]), __uint_as_float(s[q][2 * c + 1])), sl2_2, negm_2);
                         uint64_t p2;
                         if (((q * 16 + c) & (kEmuPeriod - 1)) < kEmuPairs128) {
-                            p2 = exp2_poly_x2<false>(x2);
+                            p2 = exp2_poly_x2(x2);
                         } else {
                             float x0, x1;
                             f2_unpack(x2, x0, x1);

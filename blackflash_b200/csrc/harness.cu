@@ -84,7 +84,7 @@ static bool load_file(const char* dir, const char* name, void* dst, size_t bytes
 int main(int argc, char** argv) {
     const char* dir = argc > 1 ? argv[1] : "ref_data";
     const int iters = argc > 2 ? atoi(argv[2]) : 10;
-    const double peak = argc > 3 ? atof(argv[3]) : 1646.1;  // measured dense bf16 TFLOP/s on this pool's B200s
+    const double peak = argc > 3 ? atof(argv[3]) : 0.0;  // optional: the device's dense bf16 TFLOP/s, for a percentage
     int B = 0, H = 0, N = 0, d = 0;
     float scale = 0.f;
     if (!parse_meta(dir, B, H, N, d, scale)) return 1;
@@ -130,7 +130,10 @@ int main(int argc, char** argv) {
     ms /= (float)(iters > 0 ? iters : 1);
     const double fl = 4.0 * B * H * (double)N * N * d;
     const double tflops = fl / (ms * 1e-3) / 1e12;
-    printf("avg latency %.4f ms, %.2f TFLOPS, %.1f%% of %.1f TFLOPS\n", ms, tflops, 100.0 * tflops / peak, peak);
+    if (peak > 0.0)
+        printf("avg latency %.4f ms, %.2f TFLOPS, %.1f%% of %.1f TFLOPS\n", ms, tflops, 100.0 * tflops / peak, peak);
+    else
+        printf("avg latency %.4f ms, %.2f TFLOPS\n", ms, tflops);
 
     CK(cudaMemcpy(ho.data(), dout, n_qkv * 2, cudaMemcpyDeviceToHost));
     std::vector<float> hl(n_rows);

@@ -10,7 +10,10 @@
 // not pass the array's name to a kernel: on the host that name is only a stand-in
 // for the symbol, not a device address. The device address is looked up with
 // cudaGetSymbolAddress once per device, with that device current, on the first
-// call made on that device; make that first call before any stream capture.
+// call made on that device; make that first call before any stream capture. The
+// address is kept for the life of the process: after cudaDeviceReset (or any other
+// teardown of the device's primary context) it is stale, so a process that resets a
+// device must not call this entry point on it again.
 //
 // Every call on a device shares the one array and finds the previous call's data
 // in it. The backward clears the part that must start at zero (the fp32 dQ

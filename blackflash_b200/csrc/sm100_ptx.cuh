@@ -395,17 +395,9 @@ constexpr float kExp2C1 = 0.6932609677314758f;
 constexpr float kExp2C2 = 0.24261054396629333f;
 constexpr float kExp2C3 = 0.05517132207751274f;
 
-// kClampHigh: also clamp at +64 so an oversized argument gives a large finite value
-// (2^64) instead of a wrapped exponent; callers that detect overflow from the row
-// sum need this.
-template <bool kClampHigh = false>
 __device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x2) {
     float x0, x1;
     f2_unpack(x2, x0, x1);
-    if (kClampHigh) {
-        x0 = fminf(x0, 64.f);
-        x1 = fminf(x1, 64.f);
-    }
     x2 = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
     const uint64_t magic = f2_pack(12582912.f, 12582912.f);  // 1.5 * 2^23: x + magic rounds x to an integer
     const uint64_t t = f2_add(x2, magic);

@@ -111,6 +111,17 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
     return (out, lse_acc) if return_lse else out
 
 
+def bidirectional_schedule(world: int, rank: int) -> list[list[int]]:
+    """The KV blocks (by owning rank) that `_ring_bidirectional` computes at each step
+    on `rank`: [rank] first, then [r-s, r+s] for s = 1..nr and [r-s] for the one
+    extra left step when G is even (nl = floor(G/2), nr = ceil(G/2) - 1)."""
+    nl, nr = world // 2, (world + 1) // 2 - 1
+    steps = [[rank]]
+    for s in range(1, nl + 1):
+        steps.append([(rank - s) % world] + ([(rank + s) % world] if s <= nr else []))
+    return steps
+
+
 def _ring_bidirectional(q, k, v, scale, group, world, rank, partial_fn, partial_blocks_fn, merge_fn, finalize_fn,
                         return_lse):
     """Both-way KV rotation (world >= 3). Blocks r-1 .. r-nl come from the left,

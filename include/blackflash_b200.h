@@ -99,7 +99,9 @@ int blackflash_bwd(const void* Q, const void* K, const void* V, const void* O, c
  * 64 MiB array inside the library on every device that loads it, so
  * B * H * N is limited to about 250000 rows (larger problems get BF_ERR_ARG and
  * belong to blackflash_bwd). The first call on a device looks up the array's
- * device address; make it before any stream capture. All calls on a device share
+ * device address; make it before any stream capture. That address is kept until
+ * the process exits, so do not call this again on a device after cudaDeviceReset.
+ * All calls on a device share
  * the array: calls in order on one stream are fine, calls that overlap on the
  * GPU race. Arguments as blackflash_bwd.
  */
@@ -126,29 +128,6 @@ int blackflash_f32_to_bf16(const float* src, void* dst, long long n, void* strea
  * site that did. With reset != 0 the word is cleared after it is read.
  */
 int blackflash_status(int reset, unsigned* out);
-
-/*
- * Test hook: the same launch as blackflash_fwd, except that the producer never
- * issues the K loads. The consumers' bounded waits therefore run out after
- * timeout_ns, the kernel returns early, and blackflash_status reports the
- * site. No fault or hang is involved. O is left undefined.
- */
-int blackflash_fwd_timeout_probe(const void* Q, const void* K, const void* V, void* O, int B, int H, int N, int d,
-                                 float scale, unsigned long long timeout_ns, void* stream);
-
-/* Test hook: raw fp32 S = Q K^T of the first 128x128 tile (CTA 0), written to dbg_s. */
-int blackflash_fwd_debug_s(const void* Q, const void* K, const void* V, void* O, float* dbg_s, int B, int H, int N,
-                           int d, float scale, void* stream);
-
-/*
- * Diagnostic hook: the same launch as blackflash_fwd, built with pipeline event
- * stamps. For CTA `trace_cta` it writes clock64() offsets into trace[4 * 512]
- * (int64, caller-zeroed): trace[role * 512 + step * 8 + event] for the CTA's
- * first 64 KV steps, roles 0/1 = softmax warpgroups, 2 = MMA issuer, 3 = TMA
- * producer. No counterpart in the reference.
- */
-int blackflash_fwd_trace(const void* Q, const void* K, const void* V, void* O, long long* trace, int trace_cta, int B,
-                         int H, int N, int d, float scale, void* stream);
 
 /* Message for the last error returned on this thread ("" if none). */
 const char* blackflash_last_error(void);

@@ -25,8 +25,15 @@ CASES = [
 ]
 
 
+def reference_dir() -> str:
+    """The reference checkout: $BLACKFLASH_REFERENCE, else a "reference" directory beside
+    this repository."""
+    repo = os.path.dirname(os.path.dirname(HERE))
+    return os.environ.get("BLACKFLASH_REFERENCE") or os.path.join(os.path.dirname(repo), "reference")
+
+
 def main() -> None:
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else reference_dir()
     script = os.path.join(ref, "profile", "gen_ref.py")
     for B, H, N, seed in CASES:
         out = os.path.join(HERE, f"gen_ref_b{B}h{H}n{N}")

@@ -19,7 +19,7 @@ def read_meta(path: str) -> dict:
         for line in f:
             if "=" in line:
                 k, v = line.strip().split("=", 1)
-                meta[k] = float(v) if k == "scale" else int(v)
+                meta[k] = float(v) if k == "scale" else (int(v) if v.lstrip("-").isdigit() else v)
     return meta
 
 

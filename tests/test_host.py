@@ -16,7 +16,9 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _header_functions():
-    text = open(os.path.join(REPO, "include", "blackflash_b200.h")).read()
+    """Functions declared by the C ABI header and the diagnostic-hooks header."""
+    text = "".join(open(os.path.join(REPO, "include", h)).read()
+                   for h in ("blackflash_b200.h", "blackflash_b200_diag.h"))
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(blackflash_\w+)\s*\(", text)))
 

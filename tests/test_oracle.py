@@ -102,3 +102,29 @@ def test_backward_oracle_matches_torch_autograd(B, H, N, d):
     dq, dk, dv = oracle.attn_bwd(q, k, v, do, scale)
     for got, ref in ((dq, qf.grad), (dk, kf.grad), (dv, vf.grad)):
         np.testing.assert_allclose(got, ref.numpy(), rtol=1e-5, atol=1e-6)
+
+
+def test_ref_data_writer_format(tmp_path):
+    """tests/golden/make_ref_data.py writes gen_ref's layout (readable by golden_io) with
+    the distribution keys, and its o_ref is the bf16 rounding of the torch fp32 formula."""
+    import os
+    import sys
+
+    import torch
+    from golden_io import GOLDEN_DIR, read_meta
+    sys.path.insert(0, GOLDEN_DIR)
+    from make_ref_data import write_ref_data
+    out = str(tmp_path / "rd")
+    write_ref_data(out, 1, 2, 96, dist="peaked", seed=3)
+    m = read_meta(out)
+    assert m["dist_q"] == "normal(0,3)" and m["dist_v"] == "uniform(-1,1)" and m["seed"] == 3
+    shape = (m["B"], m["H"], m["N"], m["d"])
+    assert shape == (1, 2, 96, 64) and abs(m["scale"] - 0.125) < 1e-9
+
+    def bf16(fn):
+        raw = np.fromfile(os.path.join(out, fn), dtype="<u2").reshape(shape)
+        return torch.from_numpy(raw.astype(np.int16)).view(torch.bfloat16)
+    q, k, v, o = (bf16(f) for f in ("q.bin", "k.bin", "v.bin", "o_ref.bin"))
+    ref = oracle.torch_math(q, k, v, 0.125)
+    assert (o.float() - ref).abs().max().item() <= 1e-2  # one bf16 rounding of |O| <= 1
+    assert not os.path.exists(os.path.join(out, "s_ref.bin"))

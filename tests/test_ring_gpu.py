@@ -114,7 +114,7 @@ def _ring_worker(rank, world, port, qkv, out, mode="ring"):
 @pytest.mark.parametrize("mode", ["ring", "ring1", "allgather"])
 def test_ring_over_nccl(tmp_path, mode):
     from blackflash_b200.inputs import make_qkv
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)  # at 8 ranks the both-way ring runs nl=4, nr=3
     S, N = 4, 512 * world
     q, k, v = (t.reshape(S, N, 64) for t in make_qkv(1, S, N, seed=77))
     out = str(tmp_path / "ring")
@@ -123,3 +123,49 @@ def test_ring_over_nccl(tmp_path, mode):
     o_ref, _, _ = oracle.attn_exact(q, k, v, 0.125)
     d = np.abs(o - o_ref)
     assert d.max() <= 1e-2 and d.mean() <= 1e-3
+
+
+def test_config5_per_rank_schedules_on_one_gpu():
+    """BASELINE config 5 (B=1 H=32 N=65536, N(0,1)) at its own shape: every per-rank
+    computation of the 8-rank both-way ring (own block, then the pairs L_s / R_s in one
+    gathered-block launch each, merged step by step in `bidirectional_schedule` order)
+    and of the all-gather schedule (own block + one launch over the other 7 blocks),
+    run in one process on one GPU. Sampled query rows of three heads on three ranks
+    are checked against the oracle over all 65536 keys; every rank's two schedules must
+    agree with each other."""
+    from blackflash_b200 import attention_partial, attention_partial_blocks, lse_merge_, to_bf16
+    from blackflash_b200.inputs import make_qkv
+    from blackflash_b200.ring import bidirectional_schedule
+    H, N, G = 32, 65536, 8
+    n = N // G
+    q, k, v = (t.reshape(H, N, 64) for t in make_qkv(1, H, N, seed=5005, device="cuda"))
+    kb = torch.stack([k[:, r * n:(r + 1) * n] for r in range(G)])  # [G, H, n, 64], as all-gathered
+    vb = torch.stack([v[:, r * n:(r + 1) * n] for r in range(G)])
+    heads, rows = [0, 13, 31], torch.arange(0, n, 32)[:256]
+    for r in range(G):
+        qr = q[:, r * n:(r + 1) * n].contiguous()
+        steps = bidirectional_schedule(G, r)
+        assert sorted(b for st in steps for b in st) == list(range(G))
+        o_acc, lse_acc = attention_partial(qr, kb[r], vb[r], 0.125)
+        for st in steps[1:]:
+            if len(st) == 2:
+                o_p, l_p = attention_partial_blocks(qr, kb[st].contiguous(), vb[st].contiguous(), 0.125, -1)
+            else:
+                o_p, l_p = attention_partial(qr, kb[st[0]], vb[st[0]], 0.125)
+            lse_merge_(o_acc, lse_acc, o_p, l_p)
+        o_ring = to_bf16(o_acc)
+        o_ag, lse_ag = attention_partial(qr, kb[r], vb[r], 0.125)
+        o_rem, l_rem = attention_partial_blocks(qr, kb, vb, 0.125, r)
+        lse_merge_(o_ag, lse_ag, o_rem, l_rem)
+        o_ag = to_bf16(o_ag)
+        torch.cuda.synchronize()
+        assert (o_ring.float() - o_ag.float()).abs().max().item() <= 4e-3
+        assert (lse_acc - lse_ag).abs().max().item() <= 1e-3
+        if r not in (0, 3, 7):
+            continue
+        for h in heads:
+            o_ref, lse_ref, _ = oracle.attn_exact(qr[h, rows].cpu(), k[h].cpu(), v[h].cpu(), 0.125)
+            for o in (o_ring, o_ag):
+                d = np.abs(o[h, rows].float().cpu().numpy() - o_ref)
+                assert d.max() <= 1e-2 and d.mean() <= 1e-3, (r, h, d.max(), d.mean())
+            np.testing.assert_allclose(lse_acc[h, rows].cpu().numpy(), lse_ref, atol=2e-3)

@@ -47,6 +47,7 @@
 #include <string.h>
 
 #include <atomic>
+#include <utility>
 
 namespace bfk {
 
@@ -206,6 +207,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nk = (p.n_kv + kBN - 1) / kBN;
     const long long trace_t0 = kTrace ? clock64() : 0;
     const bool trace_hit = kTrace && (int)blockIdx.x == p.trace_cta;
+    // Trace builds also record, for every CTA, the global timer (ns) at entry, after the
+    // set-up, when its first S tile is ready and at exit: trace[4 * 512 + cta * 4 + k].
+    if constexpr (kTrace) {
+        if (threadIdx.x == 0) p.trace[4 * 512 + blockIdx.x * 4 + 0] = (long long)global_timer_ns();
+    }
 
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2; ++b) {
@@ -244,6 +250,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
     const WaitCtl ctl{&bars->abort_flag, &g_wait_status, p.timeout_ns};
+    // The set-up above (barriers, TMEM, descriptor prefetch) touches no global data, so
+    // with programmatic dependent launch it overlaps the previous grid's tail; every
+    // global read or write comes after the wait. The next grid may be scheduled as soon
+    // as this one's CTAs start to exit.
+    griddep_launch_dependents();
+    griddep_wait();
+    if constexpr (kTrace) {
+        if (threadIdx.x == 0) p.trace[4 * 512 + blockIdx.x * 4 + 1] = (long long)global_timer_ns();
+    }
 
 #if BF_REGSPLIT
     // Launch budget 96 x 640 = 61440: softmax 104 x 512 + issuers 64 x 128.
@@ -295,6 +310,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!(ok = warp_wait(bar_s, g & 1u, ctl, kSiteSoftS))) break;
                 tc_fence_after();
                 BF_TRACE(t, g, 1);
+                if constexpr (kTrace) {
+                    if (g == 0 && threadIdx.x == 0) p.trace[4 * 512 + blockIdx.x * 4 + 2] = (long long)global_timer_ns();
+                }
 
                 uint32_t s[2][32];  // columns 64h + [0, 32) and 64h + [32, 64)
                 tmem_ld16x32bx2_x32<64>(tS + 0, s[0]);
@@ -637,6 +655,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if constexpr (kTrace) {
+        if (threadIdx.x == 0) p.trace[4 * 512 + blockIdx.x * 4 + 3] = (long long)global_timer_ns();
+    }
 }
 
 #include "fa_fwd_sm100_d128.cuh"
@@ -691,6 +712,62 @@ int make_map(CUtensorMap* m, const void* base, long long bh, int rows, int d = b
     return BF_OK;
 }
 
+// Tensor maps depend only on (base, slices, rows, d); the launchers ask for four per
+// call, and the encode is a driver call, so the last few are kept per host thread and
+// per device.
+struct MapCacheEntry {
+    const void* base;
+    long long bh;
+    int rows, d, dev;
+    CUtensorMap map;
+};
+constexpr int kMapCacheSize = 16;
+thread_local MapCacheEntry g_map_cache[kMapCacheSize];
+thread_local int g_map_cache_used = 0, g_map_cache_next = 0;
+
+int cached_map(CUtensorMap* m, const void* base, long long bh, int rows, int d = bfk::kD) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
+    for (int i = 0; i < g_map_cache_used; ++i) {
+        const MapCacheEntry& e = g_map_cache[i];
+        if (e.base == base && e.bh == bh && e.rows == rows && e.d == d && e.dev == dev) {
+            *m = e.map;
+            return BF_OK;
+        }
+    }
+    const int rc = make_map(m, base, bh, rows, d);
+    if (rc != BF_OK) return rc;
+    MapCacheEntry& e = g_map_cache[g_map_cache_next];
+    e.base = base;
+    e.bh = bh;
+    e.rows = rows;
+    e.d = d;
+    e.dev = dev;
+    e.map = *m;
+    g_map_cache_next = (g_map_cache_next + 1) % kMapCacheSize;
+    if (g_map_cache_used < kMapCacheSize) ++g_map_cache_used;
+    return BF_OK;
+}
+
+// Launch with programmatic stream serialisation: the kernel's set-up overlaps the tail
+// of the previous kernel on the stream (the kernels wait with griddepcontrol.wait
+// before touching global memory).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <bool kF32Out>
 int configure_once() {
     static std::atomic<bool> done[64];  // per device; zero-initialised (static storage)
@@ -742,9 +819,9 @@ int bf_fwd_launch(const BfFwdArgs* a) {
     if (a->d == bfk::d128::kD) {
         if (!a->o || a->o_f32 || a->kv_blocks || a->trace || a->dbg_s || a->skip_k_loads)
             return bf_set_error(BF_ERR_ARG, "d=128 supports the bf16 forward (causal, lse and row max optional) only");
-        if ((rc = make_map(&mq, a->q, a->bh, a->n_q, 128)) != BF_OK) return rc;
-        if ((rc = make_map(&mk, a->k, a->bh, a->n_kv, 128)) != BF_OK) return rc;
-        if ((rc = make_map(&mv, a->v, a->bh, a->n_kv, 128)) != BF_OK) return rc;
+        if ((rc = cached_map(&mq, a->q, a->bh, a->n_q, 128)) != BF_OK) return rc;
+        if ((rc = cached_map(&mk, a->k, a->bh, a->n_kv, 128)) != BF_OK) return rc;
+        if ((rc = cached_map(&mv, a->v, a->bh, a->n_kv, 128)) != BF_OK) return rc;
         bfk::KParams kp;
         memset(&kp, 0, sizeof(kp));
         kp.n_q = a->n_q;
@@ -768,14 +845,13 @@ int bf_fwd_launch(const BfFwdArgs* a) {
             if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
             done[dev] = true;
         }
-        bfk::d128::fa_fwd_d128_kernel<<<(unsigned)grid, bfk::kThreads, bfk::d128::kSmemBytes,
-                                       reinterpret_cast<cudaStream_t>(a->stream)>>>(
-            mq, mk, mv, reinterpret_cast<__nv_bfloat16*>(a->o), kp);
-        const cudaError_t e = cudaGetLastError();
+        const cudaError_t e =
+            launch_pdl(bfk::d128::fa_fwd_d128_kernel, (unsigned)grid, bfk::kThreads, bfk::d128::kSmemBytes,
+                       reinterpret_cast<cudaStream_t>(a->stream), mq, mk, mv, reinterpret_cast<__nv_bfloat16*>(a->o), kp);
         if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
         return BF_OK;
     }
-    if ((rc = make_map(&mq, a->q, a->bh, a->n_q)) != BF_OK) return rc;
+    if ((rc = cached_map(&mq, a->q, a->bh, a->n_q)) != BF_OK) return rc;
     int kv_blk_tiles = 0;
     if (a->kv_blocks) {
         if (a->kv_blocks < 1 || a->kv_block_rows <= 0 || a->kv_block_rows % bfk::kBN ||
@@ -785,14 +861,14 @@ int bf_fwd_launch(const BfFwdArgs* a) {
             return bf_set_error(BF_ERR_ARG, "blocked KV: n_kv must equal the rows of the blocks used");
         if ((long long)a->kv_blocks * a->bh > 0x7fffffffLL) return bf_set_error(BF_ERR_ARG, "problem too large for one launch");
         kv_blk_tiles = a->kv_block_rows / bfk::kBN;
-        if ((rc = make_map(&mk, a->k, (long long)a->kv_blocks * a->bh, a->kv_block_rows)) != BF_OK) return rc;
-        if ((rc = make_map(&mv, a->v, (long long)a->kv_blocks * a->bh, a->kv_block_rows)) != BF_OK) return rc;
+        if ((rc = cached_map(&mk, a->k, (long long)a->kv_blocks * a->bh, a->kv_block_rows)) != BF_OK) return rc;
+        if ((rc = cached_map(&mv, a->v, (long long)a->kv_blocks * a->bh, a->kv_block_rows)) != BF_OK) return rc;
     } else {
-        if ((rc = make_map(&mk, a->k, a->bh, a->n_kv)) != BF_OK) return rc;
-        if ((rc = make_map(&mv, a->v, a->bh, a->n_kv)) != BF_OK) return rc;
+        if ((rc = cached_map(&mk, a->k, a->bh, a->n_kv)) != BF_OK) return rc;
+        if ((rc = cached_map(&mv, a->v, a->bh, a->n_kv)) != BF_OK) return rc;
     }
     if (a->o) {
-        if ((rc = make_map(&mo, a->o, a->bh, a->n_q)) != BF_OK) return rc;
+        if ((rc = cached_map(&mo, a->o, a->bh, a->n_q)) != BF_OK) return rc;
     } else {
         mo = mq;  // not read in fp32-output mode
     }
@@ -831,10 +907,14 @@ int bf_fwd_launch(const BfFwdArgs* a) {
         bfk::fa_fwd_sm100_kernel<false, true><<<(unsigned)grid, bfk::kThreads, bfk::kSmemBytes, stream>>>(mq, mk, mv, mo, kp);
     } else if (a->o_f32) {
         if ((rc = configure_once<true>()) != BF_OK) return rc;
-        bfk::fa_fwd_sm100_kernel<true><<<(unsigned)grid, bfk::kThreads, bfk::kSmemBytes, stream>>>(mq, mk, mv, mo, kp);
+        const cudaError_t e = launch_pdl(bfk::fa_fwd_sm100_kernel<true>, (unsigned)grid, bfk::kThreads, bfk::kSmemBytes,
+                                         stream, mq, mk, mv, mo, kp);
+        if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
     } else {
         if ((rc = configure_once<false>()) != BF_OK) return rc;
-        bfk::fa_fwd_sm100_kernel<false><<<(unsigned)grid, bfk::kThreads, bfk::kSmemBytes, stream>>>(mq, mk, mv, mo, kp);
+        const cudaError_t e = launch_pdl(bfk::fa_fwd_sm100_kernel<false>, (unsigned)grid, bfk::kThreads,
+                                         bfk::kSmemBytes, stream, mq, mk, mv, mo, kp);
+        if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));
     }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return bf_set_error(BF_ERR_CUDA, cudaGetErrorString(e));

@@ -115,6 +115,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
     const WaitCtl ctl{&bars->abort_flag, &g_wait_status, p.timeout_ns};
+    // The set-up above (barriers, TMEM, descriptor prefetch) touches no global data, so
+    // with programmatic dependent launch it overlaps the previous grid's tail; every
+    // global read or write comes after the wait. The next grid may be scheduled as soon
+    // as this one's CTAs start to exit.
+    griddep_launch_dependents();
+    griddep_wait();
 
 #if BF_REGSPLIT
     if (warp < kSoftWarps)

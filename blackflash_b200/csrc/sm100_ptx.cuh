@@ -75,13 +75,20 @@ struct WaitCtl {
     uint64_t limit_ns;
 };
 
+#ifndef BF_SLEEP_NS
+#define BF_SLEEP_NS 0
+#endif
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl, unsigned int site) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
         // A sleeping wait issues nothing, leaving the scheduler to the warps that
         // share it (the MMA issuers in particular must not be starved).
-        if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+#if BF_SLEEP_NS > 0
+        if (mbar_try_wait_sleep(bar, parity, BF_SLEEP_NS)) return true;
+#else
+        if (mbar_try_wait(bar, parity)) return true;
+#endif
         if (*ctl.abort_flag) return false;
         if (global_timer_ns() - t0 > ctl.limit_ns) {
             *ctl.abort_flag = 1;
@@ -120,6 +127,16 @@ __device__ __forceinline__ bool warp_wait_n(int n, uint32_t b0, uint32_t p0, uin
     }
     return __all_sync(0xffffffffu, ok);
 }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// launch_dependents lets the next grid of the stream (when it was launched with
+// programmatic stream serialisation) start its CTAs as this grid's CTAs exit; wait
+// blocks until every grid this one depends on has completed and its memory
+// operations are visible. Both are no-ops for a grid launched without the attribute.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {

@@ -29,10 +29,12 @@ int blackflash_fwd_debug_s(const void* Q, const void* K, const void* V, void* O,
 
 /*
  * Diagnostic hook: the same launch as blackflash_fwd, built with pipeline event
- * stamps. For CTA `trace_cta` it writes clock64() offsets into trace[4 * 512]
+ * stamps. For CTA `trace_cta` it writes clock64() offsets into trace[0, 4 * 512)
  * (int64, caller-zeroed): trace[role * 512 + step * 8 + event] for the CTA's
  * first 64 KV steps, roles 0/1 = softmax warpgroups, 2 = MMA issuer, 3 = TMA
- * producer. No counterpart in the reference.
+ * producer. For every CTA c it also writes the global timer (ns) at entry, after
+ * set-up, when its first S tile is ready and at exit into trace[4 * 512 + 4 c + k],
+ * so the buffer holds 4 * 512 + 4 * (number of SMs) entries.
  */
 int blackflash_fwd_trace(const void* Q, const void* K, const void* V, void* O, long long* trace, int trace_cta, int B,
                          int H, int N, int d, float scale, void* stream);

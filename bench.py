@@ -47,6 +47,8 @@ CONFIGS = {
     "5": (1, 32, 65536, 64, "normal"),
     # profiling case: same per-slice shape as config 3, 1/4 of the slices (1.6 GB device memory)
     "prof": (16, 64, 1024, 64, "normal"),
+    # one rank's share of config 3 at 8 GPUs (512 slices), run on one GPU
+    "r8": (8, 64, 1024, 64, "normal"),
     # head dimension 128 (extension; the reference kernel is d = 64 only)
     "d128": (16, 16, 4096, 128, "normal"),
     # attention backward (extension), d = 64: a main case and a small profiling case
@@ -454,6 +456,7 @@ def run_ours(args, cfg_name):
 SP_DESC = {
     "ring": "ring{world}: KV rotated both ways round the ring by NCCL send/recv, two blocks per step in one kernel, LSE merge per step",
     "ring1": "ring{world}: KV rotated one way by NCCL send/recv, one block per step, LSE merge per step",
+    "ipc": "ring{world}: KV rotated both ways by peer copies over CUDA IPC (copy engines, NVLink), GPU-side flags, C++ driver, LSE merge per step",
     "allgather": "sp{world}: NCCL all-gather of K/V overlapping the own-block kernel, one gathered-block kernel, one LSE merge",
 }
 
@@ -462,6 +465,12 @@ def sp_launches(mode: str, w: int) -> int:
     """Our kernels per step (partials, merges, the bf16 cast)."""
     if mode == "allgather":
         return 4 if w > 1 else 2
+    if mode == "ipc" and w > 1:
+        nl, nr = w // 2, (w + 1) // 2 - 1
+        compute = 1 + 3 * nl + nr + 1                               # partials, flag waits, merges, cast
+        copies = (3 * nl - 1) + (3 * nr - 1 if nr > 0 else 0)      # flag waits and sets of the two push streams
+        signals = nl + nr + 2                                       # slot-free flag sets
+        return compute + copies + signals
     if mode == "ring" and w > 2:
         return 1 + 2 * (w // 2) + 1
     return 2 * w
@@ -475,10 +484,12 @@ def run_ring(args, cfg_name):
     import torch.distributed as dist_mod
 
     from blackflash_b200.inputs import make_qkv
-    from blackflash_b200.ring import allgather_attention, ring_attention
+    from blackflash_b200.ring import allgather_attention, close_ipc_rings, ipc_ring_attention, ring_attention
 
     if args.sp_mode == "allgather":
         sp = allgather_attention
+    elif args.sp_mode == "ipc":
+        sp = ipc_ring_attention
     else:
         def sp(q_, k_, v_, scale_):
             return ring_attention(q_, k_, v_, scale_, bidirectional=(args.sp_mode == "ring"))
@@ -582,6 +593,8 @@ def run_ring(args, cfg_name):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        if args.sp_mode == "ipc":
+            close_ipc_rings()
         dist_mod.destroy_process_group()
 
 
@@ -597,7 +610,7 @@ def main():
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-comparators", action="store_true", help="skip the cuDNN SDPA comparison")
-    ap.add_argument("--sp-mode", choices=["ring", "ring1", "allgather"], default="ring",
+    ap.add_argument("--sp-mode", choices=["ring", "ring1", "allgather", "ipc"], default="ring",
                     help="sequence-parallel schedule of config 5")
     args = ap.parse_args()
     if args.warmup < 3:

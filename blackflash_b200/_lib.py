@@ -25,6 +25,12 @@ EXPORTED = (
     "blackflash_bwd_workspace_bytes",
     "blackflash_bwd_noalloc",
     "blackflash_status",
+    "blackflash_ring_create",
+    "blackflash_ring_handle_bytes",
+    "blackflash_ring_connect",
+    "blackflash_ring_forward",
+    "blackflash_ring_status",
+    "blackflash_ring_destroy",
     "blackflash_fwd_timeout_probe",
     "blackflash_fwd_debug_s",
     "blackflash_fwd_trace",
@@ -48,6 +54,12 @@ _SIGS = {
     "blackflash_bwd_noalloc": (_i, [_vp] * 9 + [_i, _i, _i, _i, _f, _vp]),
     "blackflash_f32_to_bf16": (_i, [_vp, _vp, _ll, _vp]),
     "blackflash_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
+    "blackflash_ring_create": (_i, [_i, _i, _ll, _i, _i, ctypes.POINTER(_vp), _vp]),
+    "blackflash_ring_handle_bytes": (_i, []),
+    "blackflash_ring_connect": (_i, [_vp, _vp]),
+    "blackflash_ring_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp]),
+    "blackflash_ring_status": (_i, [_vp, _i, ctypes.POINTER(ctypes.c_uint)]),
+    "blackflash_ring_destroy": (_i, [_vp]),
     "blackflash_fwd_timeout_probe": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, ctypes.c_ulonglong, _vp]),
     "blackflash_fwd_debug_s": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp]),
     "blackflash_fwd_trace": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp]),

@@ -21,7 +21,7 @@ HARNESS_PATH = os.path.join(LIB_DIR, "flash_attn")
 # `import blackflash_cuda` resolves as it does for the reference's installed extension.
 EXT_SRC = os.path.join(CSRC, "torch_ext.cpp")
 
-SOURCES = ["fa_fwd_sm100.cu", "capi.cu", "lse_merge.cu", "noalloc.cu"]
+SOURCES = ["fa_fwd_sm100.cu", "capi.cu", "lse_merge.cu", "noalloc.cu", "ring_ipc.cu"]
 HEADERS = ["sm100_ptx.cuh", "fa_fwd_sm100.h", "fa_fwd_sm100_d128.cuh", "fa_bwd_sm100.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", os.path.join(REPO_DIR, "include")]

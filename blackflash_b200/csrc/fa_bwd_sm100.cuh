@@ -11,22 +11,36 @@
 //   * warp 8 (TMA): K_j and V_j once; per i, Q_i and dO_i (two stages) plus the
 //     tile's 128 log2-lse and D values (bulk copies of a padded [BH, Npad] array);
 //   * warp 9 (MMA, owns TMEM):
-//       S^T  = K_j Q_i^T   (M=128 kv, N=128 q, K=64)      -> TMEM [0,128)
-//       dP^T = V_j dO_i^T  (same shape)                    -> TMEM [128,256)
+//       S^T  = K_j Q_i^T   (M=128 kv, N=128 q, K=64)      -> TMEM [0,128) or [128,256)
+//                                                            (two buffers, by i % 2)
+//       dP^T = V_j dO_i^T  (same shape)                    -> TMEM [256,384)
 //     then, once the elementwise warps have written P^T and dS^T:
-//       dV_j += P^T dO_i   (A = bf16 P^T in TMEM, S^T columns 0..63) -> TMEM [256,320)
-//       dK_j += dS^T Q_i   (A = bf16 dS^T in TMEM, S^T columns 64..127) -> TMEM [320,384)
-//       dQ_i  = dS K_j     (A = dS in shared memory, K-major) -> TMEM [384,448)
+//       dQ_i  = dS K_j     (A = dS in shared memory, K-major) -> TMEM [256,320), over
+//                                                            dP^T_i, which is read by then
+//       dV_j += P^T dO_i   (A = bf16 P^T in TMEM, S^T columns 0..63) -> TMEM [384,448)
+//       dK_j += dS^T Q_i   (A = bf16 dS^T in TMEM, S^T columns 64..127) -> TMEM [448,512)
 //   * warps 0-7 (elementwise, two threads per KV row as in the forward): P^T,
-//     dS^T into TMEM, dS into shared memory; after the MMAs, dQ_i is added to
-//     an fp32 accumulator in global memory (vector atomics), and at the end dK_j
+//     dS^T into TMEM, dS into shared memory; after the dQ product, dQ_i is added
+//     to an fp32 accumulator in global memory (vector atomics), and at the end dK_j
 //     and dV_j are written as bf16.
+// Pipelining: S^T of tile i+1 is computed (into the other buffer) while the
+// elementwise warps work on tile i, and dP^T of tile i+1 as soon as dQ_i has been
+// read out of TMEM, so the elementwise warps go from tile i's atomics straight to
+// tile i+1's exponentials. MMAs issued by one thread run in order, so S^T of tile
+// i+2 may overwrite the buffer that dV_i / dK_i read.
 // Rows past N: Q/dO/K/V rows read as zero (TMA fill), padded lse is +inf, so
 // those queries contribute nothing; KV rows past N are masked to P = 0 and
 // never stored.
 namespace bwd {
 
-constexpr int kThreadsB = 10 * 32;
+#ifndef BF_BWD_EW_REGS
+#define BF_BWD_EW_REGS 216
+#endif
+
+// Warps 10 and 11 only complete the third warpgroup, so that setmaxnreg can move
+// registers from the producer / MMA warpgroup to the elementwise warps.
+constexpr int kThreadsB = 12 * 32;
+constexpr int kEwRegs = BF_BWD_EW_REGS, kOtherRegs = 64;  // launch budget 384 x 168 = 64512
 constexpr int kEwWarps = 8;
 constexpr int kProdWarp = 8;
 constexpr int kMmaWarp = 9;
@@ -38,16 +52,18 @@ constexpr int kOffDO = kOffQ + 2 * kTile;      // [2 stages] dO_i
 constexpr int kOffDS = kOffDO + 2 * kTile;     // dS [128 q x 128 kv] K-major: 2 chunks of 64 kv
 constexpr int kOffVec = kOffDS + 2 * kTile;    // [2 stages] {lse2[128], D[128]} fp32
 constexpr int kOffBar = kOffVec + 2 * 1024;
-constexpr int kColST = 0, kColDPT = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
+constexpr int kColST = 0, kColDPT = 256, kColDQ = 256, kColDV = 384, kColDK = 448;
 
 struct Bars {
     uint64_t kv_full;
     uint64_t qd_full[2];
     uint64_t qd_empty[2];
-    uint64_t s_full;
-    uint64_t p_ready;
-    uint64_t mma_done;
-    uint64_t ew_free;
+    uint64_t s_full[2];   // S^T of the tile in buffer b computed
+    uint64_t dp_full;     // dP^T computed
+    uint64_t p_ready;     // P^T, dS^T (TMEM) and dS (smem) written, dP^T read
+    uint64_t dq_done;     // dQ_i computed (and dS_i read from shared memory)
+    uint64_t dq_free;     // dQ_i read out of TMEM
+    uint64_t acc_done;    // every dV / dK product finished
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
@@ -97,10 +113,13 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             mbar_init(smem_addr(&bars->qd_full[s]), 1);
             mbar_init(smem_addr(&bars->qd_empty[s]), 1);
         }
-        mbar_init(smem_addr(&bars->s_full), 1);
+        mbar_init(smem_addr(&bars->s_full[0]), 1);
+        mbar_init(smem_addr(&bars->s_full[1]), 1);
+        mbar_init(smem_addr(&bars->dp_full), 1);
         mbar_init(smem_addr(&bars->p_ready), kEwWarps * 32);
-        mbar_init(smem_addr(&bars->mma_done), 1);
-        mbar_init(smem_addr(&bars->ew_free), kEwWarps * 32);
+        mbar_init(smem_addr(&bars->dq_done), 1);
+        mbar_init(smem_addr(&bars->dq_free), kEwWarps * 32);
+        mbar_init(smem_addr(&bars->acc_done), 1);
         mbar_init(smem_addr(&bars->drain), 1);
         bars->abort_flag = 0;
         fence_barrier_init();
@@ -120,6 +139,12 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
     const WaitCtl ctl{&bars->abort_flag, &g_wait_status, p.timeout_ns};
+    static_assert(kEwWarps * 32 * kEwRegs + (kThreadsB - kEwWarps * 32) * kOtherRegs <= kThreadsB * 168,
+                  "register split exceeds the launch budget");
+    if (warp < kEwWarps)
+        regs_inc<kEwRegs>();
+    else
+        regs_dec<kOtherRegs>();
 
     if (warp < kEwWarps) {
         // ------------------------------------------------------------ elementwise
@@ -128,13 +153,14 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         const int h = lane >> 4;                                 // q columns 64h .. 64h + 63
         const int row = quarter * 32 + sub * 16 + (lane & 15);   // KV row in the tile == TMEM lane
         const uint32_t lane_off = (uint32_t)(quarter * 32 + sub * 16) << 16;
-        const uint32_t tST = tmem + lane_off + kColST, tDPT = tmem + lane_off + kColDPT;
+        const uint32_t tDPT = tmem + lane_off + kColDPT;
         const bool kv_ok = jt * 128 + row < p.n;
         uint8_t* ds_smem = smem + kOffDS + (row >> 6) * kTile;  // chunk holding this KV column
         const int ds_unit = (row & 63) >> 3, ds_sub = (row & 7) * 2;
         bool ok = true;
         for (int i = 0; i < p.q_tiles && ok; ++i) {
-            if (!(ok = warp_wait(smem_addr(&bars->s_full), (uint32_t)i & 1u, ctl, kSiteBEwS))) break;
+            const uint32_t tST = tmem + lane_off + kColST + (uint32_t)(i & 1) * 128;
+            if (!(ok = warp_wait(smem_addr(&bars->s_full[i & 1]), (uint32_t)(i >> 1) & 1u, ctl, kSiteBEwS))) break;
             tc_fence_after();
             const float* vec = reinterpret_cast<const float*>(smem + kOffVec + (i & 1) * 1024);
             const float* lse2 = vec + h * 64;
@@ -158,6 +184,8 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             tmem_st16x32bx2_x16<32>(tST + 16, pk + 16);
 
             // dS = P (dP - D), from the bf16 P the dV product uses (dS is rounded to bf16 too).
+            if (!(ok = warp_wait(smem_addr(&bars->dp_full), (uint32_t)i & 1u, ctl, kSiteBEwS))) break;
+            tc_fence_after();
             uint32_t dsk[32];
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
@@ -177,7 +205,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             }
             // dS [q][kv] into shared memory, 128-byte swizzled K-major rows (A of dQ = dS K).
             // Earlier readers of this buffer (dQ(i-1) = dS(i-1) K) completed before this
-            // thread observed mma_done(i-1).
+            // thread observed dq_done(i-1).
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
 #pragma unroll
@@ -193,12 +221,14 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             mbar_arrive(smem_addr(&bars->p_ready));
 
             // dQ_i (rows = queries) into the fp32 accumulator.
-            if (!(ok = warp_wait(smem_addr(&bars->mma_done), (uint32_t)i & 1u, ctl, kSiteBEwDone))) break;
+            if (!(ok = warp_wait(smem_addr(&bars->dq_done), (uint32_t)i & 1u, ctl, kSiteBEwDone))) break;
             tc_fence_after();
             {
                 uint32_t o[32];
                 tmem_ld16x32bx2_x32<32>(tmem + lane_off + kColDQ, o);
                 tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(smem_addr(&bars->dq_free));  // dP^T of the next tile may overwrite it
                 const int q_abs = i * 128 + row;
                 if (q_abs < p.n) {
                     float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((size_t)bh * p.n + q_abs) * 64 + h * 32);
@@ -208,11 +238,11 @@ __global__ void __launch_bounds__(kThreadsB, 1)
                                                        __uint_as_float(o[4 * c + 2]), __uint_as_float(o[4 * c + 3])));
                 }
             }
-            tc_fence_before();
-            mbar_arrive(smem_addr(&bars->ew_free));
         }
+        if (ok) ok = warp_wait(smem_addr(&bars->acc_done), 0u, ctl, kSiteBEwDone);
         if (ok) {
-            // dV_j and dK_j (their last MMAs completed before mma_done of the last tile).
+            tc_fence_after();
+            // dV_j and dK_j.
             const int kv_abs = jt * 128 + row;
 #pragma unroll 1
             for (int which = 0; which < 2; ++which) {
@@ -271,7 +301,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
                 mbar_wait(smem_addr(&bars->qd_full[(last - 1) & 1]), (uint32_t)((last - 1) >> 1) & 1u, drain, 0);
         }
         __syncwarp();
-    } else {
+    } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
         constexpr uint32_t kIdescT = idesc_bf16_f32(128, 128, 0);  // K-major x K-major, N = 128 queries
         constexpr uint32_t kIdescG = idesc_bf16_f32(128, 64, 1);   // A x (MN-major, N = 64 head dims)
@@ -283,41 +313,69 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         const uint32_t k_lo = lo0 + (kOffK >> 4), v_lo = lo0 + (kOffV >> 4), ds_lo = lo0 + (kOffDS >> 4);
         bool ok = warp_wait(smem_addr(&bars->kv_full), 0u, ctl, kSiteBMmaKV);
         tc_fence_after();
-        for (int i = 0; i < p.q_tiles && ok; ++i) {
-            const int s = i & 1;
-            if (!(ok = warp_wait(smem_addr(&bars->qd_full[s]), (uint32_t)(i >> 1) & 1u, ctl, kSiteBMmaQ))) break;
-            if (i > 0 && !(ok = warp_wait(smem_addr(&bars->ew_free), (uint32_t)(i - 1) & 1u, ctl, kSiteBMmaFree)))
-                break;
+        const int T = p.q_tiles;
+        auto q_lo = [&](int i) { return lo0 + ((kOffQ >> 4) + (uint32_t)(i & 1) * kTileLo); };
+        auto do_lo = [&](int i) { return lo0 + ((kOffDO >> 4) + (uint32_t)(i & 1) * kTileLo); };
+        auto wait_qd = [&](int i) {
+            const bool r = warp_wait(smem_addr(&bars->qd_full[i & 1]), (uint32_t)(i >> 1) & 1u, ctl, kSiteBMmaQ);
             tc_fence_after();
-            const uint32_t q_lo = lo0 + ((kOffQ >> 4) + s * kTileLo), do_lo = lo0 + ((kOffDO >> 4) + s * kTileLo);
+            return r;
+        };
+        auto issue_st = [&](int i) {  // S^T_i = K Q_i^T into buffer i % 2
             if (leader) {
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) umma_ss_lo(tmem + kColST, k_lo + kk * 2, q_lo + kk * 2, desc_hi, kIdescT, kk > 0);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    umma_ss_lo(tmem + kColDPT, v_lo + kk * 2, do_lo + kk * 2, desc_hi, kIdescT, kk > 0);
-                umma_commit(smem_addr(&bars->s_full));
+                    umma_ss_lo(tmem + kColST + (uint32_t)(i & 1) * 128, k_lo + kk * 2, q_lo(i) + kk * 2, desc_hi, kIdescT,
+                               kk > 0);
+                umma_commit(smem_addr(&bars->s_full[i & 1]));
             }
             __syncwarp();
-            if (!(ok = warp_wait(smem_addr(&bars->p_ready), (uint32_t)i & 1u, ctl, kSiteBMmaP))) break;
-            tc_fence_after();
+        };
+        auto issue_dpt = [&](int i) {  // dP^T_i = V dO_i^T
             if (leader) {
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)  // 16 queries per step: 8 TMEM columns of P^T, 16 x 128 B of dO
-                    umma_ts_lo(tmem + kColDV, tmem + kColST + kk * 8, do_lo + kk * 128, desc_hi, kIdescG,
-                               (i > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    umma_ts_lo(tmem + kColDK, tmem + kColST + 64 + kk * 8, q_lo + kk * 128, desc_hi, kIdescG,
-                               (i > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_ss_lo(tmem + kColDPT, v_lo + kk * 2, do_lo(i) + kk * 2, desc_hi, kIdescT, kk > 0);
+                umma_commit(smem_addr(&bars->dp_full));
+            }
+            __syncwarp();
+        };
+        if (ok && (ok = wait_qd(0))) {
+            issue_st(0);
+            issue_dpt(0);
+            if (T > 1 && (ok = wait_qd(1))) issue_st(1);
+        }
+        for (int i = 0; i < T && ok; ++i) {
+            if (!(ok = warp_wait(smem_addr(&bars->p_ready), (uint32_t)i & 1u, ctl, kSiteBMmaP))) break;
+            tc_fence_after();
+            const uint32_t st_col = tmem + kColST + (uint32_t)(i & 1) * 128;
+            if (leader) {
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)  // 16 KV rows per step: dS chunk (kk / 4), K rows 16 kk
                     umma_ss_lo(tmem + kColDQ, ds_lo + (uint32_t)(kk >> 2) * kTileLo + (uint32_t)(kk & 3) * 2,
                                k_lo + kk * 128, desc_hi, kIdescG, kk > 0);
-                umma_commit(smem_addr(&bars->mma_done));
-                umma_commit(smem_addr(&bars->qd_empty[s]));
+                umma_commit(smem_addr(&bars->dq_done));
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)  // 16 queries per step: 8 TMEM columns of P^T, 16 x 128 B of dO
+                    umma_ts_lo(tmem + kColDV, st_col + kk * 8, do_lo(i) + kk * 128, desc_hi, kIdescG,
+                               (i > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_ts_lo(tmem + kColDK, st_col + 64 + kk * 8, q_lo(i) + kk * 128, desc_hi, kIdescG,
+                               (i > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(smem_addr(&bars->qd_empty[i & 1]));
+                if (i == T - 1) umma_commit(smem_addr(&bars->acc_done));
             }
             __syncwarp();
+            if (i + 1 < T) {
+                if (!(ok = warp_wait(smem_addr(&bars->dq_free), (uint32_t)i & 1u, ctl, kSiteBMmaFree))) break;
+                tc_fence_after();
+                issue_dpt(i + 1);
+            }
+            if (i + 2 < T) {
+                if (!(ok = wait_qd(i + 2))) break;
+                issue_st(i + 2);
+            }
         }
         if (leader) umma_commit(smem_addr(&bars->drain));
         __syncwarp();

@@ -205,3 +205,82 @@ def allgather_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale
     merge_fn(o_acc, lse_acc, o_rem, lse_rem)
     out = finalize_fn(o_acc)
     return (out, lse_acc) if return_lse else out
+
+
+class _IpcRing:
+    """A blackflash_ring_* context (csrc/ring_ipc.cu) for one (group, shape, device)."""
+
+    def __init__(self, group, world: int, rank: int, bh: int, n: int, device: torch.device):
+        import ctypes
+
+        from . import _lib
+        self.lib = _lib.load()
+        hb = self.lib.blackflash_ring_handle_bytes()
+        handle = ctypes.create_string_buffer(hb)
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check(self.lib.blackflash_ring_create(world, rank, bh, n, 64, ctypes.byref(ptr), handle),
+                       "blackflash_ring_create")
+        self.ptr = ptr
+        handles = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        allh = ctypes.create_string_buffer(b"".join(handles), hb * world)
+        with torch.cuda.device(device):
+            _lib.check(self.lib.blackflash_ring_connect(self.ptr, allh), "blackflash_ring_connect")
+        dist.barrier(group=group)  # every rank has opened its neighbours' buffers
+
+    def __call__(self, q, k, v, scale, return_lse):
+        from . import _lib
+        out = torch.empty_like(q)
+        lse = torch.empty(q.shape[:2], dtype=torch.float32, device=q.device) if return_lse else None
+        with torch.cuda.device(q.device):
+            rc = self.lib.blackflash_ring_forward(self.ptr, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                                  lse.data_ptr() if lse is not None else None, float(scale),
+                                                  torch.cuda.current_stream(q.device).cuda_stream)
+        _lib.check(rc, "blackflash_ring_forward")
+        return (out, lse) if return_lse else out
+
+    def status(self) -> int:
+        import ctypes
+        v = ctypes.c_uint(0)
+        self.lib.blackflash_ring_status(self.ptr, 1, ctypes.byref(v))
+        return v.value
+
+    def close(self):
+        if self.ptr is not None:
+            self.lib.blackflash_ring_destroy(self.ptr)
+            self.ptr = None
+
+
+_IPC_RINGS: dict = {}
+
+
+def ipc_ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, group=None,
+                       return_lse: bool = False):
+    """Same result as `ring_attention` (both-way schedule), with the KV rotation done by
+    peer copies into the neighbours' memory over CUDA IPC (copy engines on NVLink) and
+    GPU-side flags, all driven from C++ (blackflash_ring_forward). One process per GPU
+    of one node; q, k, v: [S, n, 64] bf16 with n a multiple of 128. The ring context
+    (buffers, IPC mappings) is created on first use for this group, shape and device
+    and kept for later calls; `close_ipc_rings()` frees it."""
+    world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+    if world == 1:
+        return allgather_attention(q, k, v, scale, group=group, return_lse=return_lse)
+    rank = dist.get_rank(group)
+    if k.shape != v.shape or q.shape != k.shape or q.shape[-1] != 64:
+        raise RuntimeError("ipc_ring_attention: q, k, v must all be [S, n, 64]")
+    for t in (q, k, v):
+        if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()):
+            raise RuntimeError("ipc_ring_attention: q, k, v must be contiguous CUDA bfloat16 tensors")
+    key = (id(group), world, rank, q.shape[0], q.shape[1], q.device)
+    ring = _IPC_RINGS.get(key)
+    if ring is None:
+        ring = _IPC_RINGS[key] = _IpcRing(group, world, rank, q.shape[0], q.shape[1], q.device)
+    return ring(q, k, v, scale, return_lse)
+
+
+def close_ipc_rings():
+    """Free every ring context this process created (collective: call on all ranks)."""
+    for r in _IPC_RINGS.values():
+        r.close()
+    _IPC_RINGS.clear()

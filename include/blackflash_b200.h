@@ -6,7 +6,8 @@
  * as `void*`. Calls are asynchronous on that stream. They return BF_OK or an
  * error code, and blackflash_last_error() gives the message for the calling
  * thread. No entry point allocates device memory or synchronises the device,
- * except the ones documented as synchronous (blackflash_status).
+ * except blackflash_ring_create / blackflash_ring_destroy (which own the ring's
+ * buffers) and the ones documented as synchronous (the status reads).
  *
  * Layouts: Q, K, V and O are contiguous [B, H, N, d] bf16, d = 64 or 128 (the same layout as
  * the reference, binding/blackflash_ops.cu:24-27). lse and row_max are [B, H, N]
@@ -120,6 +121,34 @@ int blackflash_lse_merge(float* O_acc, float* lse_acc, const float* O_part, cons
 
 /* fp32 -> bf16 (round to nearest even), n elements. */
 int blackflash_f32_to_bf16(const float* src, void* dst, long long n, void* stream);
+
+/*
+ * Sequence-parallel forward over G processes (one per GPU of a node), KV blocks
+ * moved round the ring in both directions by peer copies into the neighbours'
+ * memory (CUDA IPC, copy engines over NVLink) and merged by log-sum-exp. The
+ * schedule of the NCCL ring in blackflash_b200/ring.py, driven from C++ with
+ * GPU-side flags; no counterpart in the reference, which has no multi-GPU mode.
+ *   1. blackflash_ring_create(world, rank, BH, n, 64, &ring, handle): allocates
+ *      the ring's buffers on the current device (two receive slots of two K and
+ *      two V blocks, fp32 accumulators) and writes this rank's IPC handle
+ *      (blackflash_ring_handle_bytes() bytes). n: rows per rank, a multiple of 128.
+ *   2. Exchange the handles (all ranks' handles, concatenated in rank order) and
+ *      call blackflash_ring_connect(ring, handles).
+ *   3. blackflash_ring_forward(ring, Q, K, V, O, lse, scale, stream), collectively:
+ *      Q, K, V [BH, n, 64] bf16 are this rank's rows; O [BH, n, 64] bf16 and lse
+ *      [BH, n] fp32 (optional) receive this rank's rows of the full attention.
+ *      Asynchronous on `stream`; K and V must stay unchanged until it completes.
+ *   blackflash_ring_status reads (and optionally clears) the ring's wait-timeout
+ *   word: a wait on a neighbour that gave up after 10 s gives BF_ERR_TIMEOUT.
+ *   blackflash_ring_destroy synchronises the device and frees everything.
+ */
+int blackflash_ring_handle_bytes(void);
+int blackflash_ring_create(int world, int rank, long long BH, int n, int d, void** ring, void* handle_out);
+int blackflash_ring_connect(void* ring, const void* handles);
+int blackflash_ring_forward(void* ring, const void* Q, const void* K, const void* V, void* O, float* lse, float scale,
+                            void* stream);
+int blackflash_ring_status(void* ring, int reset, unsigned* out);
+int blackflash_ring_destroy(void* ring);
 
 /*
  * Wait-timeout status of the current device. It is synchronous: it reads a

@@ -96,13 +96,21 @@ def _ring_worker(rank, world, port, qkv, out, mode="ring"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
-    from blackflash_b200.ring import allgather_attention, ring_attention
+    from blackflash_b200.ring import allgather_attention, close_ipc_rings, ipc_ring_attention, ring_attention
     q, k, v = (t.cuda() for t in qkv)
     n = q.shape[1] // world
     sl = slice(rank * n, (rank + 1) * n)
     args = (q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), 0.125)
     if mode == "allgather":
         o = allgather_attention(*args)
+    elif mode == "ipc":
+        # Two calls on the same ring context: the second (V negated) must not see the
+        # first call's blocks; O is linear in V.
+        o2 = ipc_ring_attention(args[0], args[1], (-args[2]).contiguous(), 0.125)
+        o = ipc_ring_attention(*args)
+        torch.cuda.synchronize()
+        assert torch.equal(o2, -o), "second call on the ring saw stale data"
+        close_ipc_rings()
     else:
         o = ring_attention(*args, bidirectional=(mode == "ring"))
     torch.save(o.cpu(), f"{out}.{rank}")
@@ -111,7 +119,7 @@ def _ring_worker(rank, world, port, qkv, out, mode="ring"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
-@pytest.mark.parametrize("mode", ["ring", "ring1", "allgather"])
+@pytest.mark.parametrize("mode", ["ring", "ring1", "allgather", "ipc"])
 def test_ring_over_nccl(tmp_path, mode):
     from blackflash_b200.inputs import make_qkv
     world = min(torch.cuda.device_count(), 8)  # at 8 ranks the both-way ring runs nl=4, nr=3

@@ -20,9 +20,11 @@
 //       dV_j += P^T dO_i   (A = bf16 P^T in TMEM, S^T columns 0..63) -> TMEM [384,448)
 //       dK_j += dS^T Q_i   (A = bf16 dS^T in TMEM, S^T columns 64..127) -> TMEM [448,512)
 //   * warps 0-7 (elementwise, two threads per KV row as in the forward): P^T,
-//     dS^T into TMEM, dS into shared memory; after the dQ product, dQ_i is added
-//     to an fp32 accumulator in global memory (vector atomics), and at the end dK_j
-//     and dV_j are written as bf16.
+//     dS^T into TMEM, dS into shared memory; after the dQ product, dQ_i goes to a
+//     swizzled shared-memory stage and one thread adds it to the fp32 accumulator in
+//     global memory with two TMA reduce-adds (the TMA unit does the read-modify-write;
+//     rows past N are clipped by the tensor map); at the end dK_j and dV_j are
+//     written as bf16.
 // Pipelining: S^T of tile i+1 is computed (into the other buffer) while the
 // elementwise warps work on tile i, and dP^T of tile i+1 as soon as dQ_i has been
 // read out of TMEM, so the elementwise warps go from tile i's atomics straight to
@@ -51,7 +53,8 @@ constexpr int kOffQ = kOffV + kTile;           // [2 stages] Q_i
 constexpr int kOffDO = kOffQ + 2 * kTile;      // [2 stages] dO_i
 constexpr int kOffDS = kOffDO + 2 * kTile;     // dS [128 q x 128 kv] K-major: 2 chunks of 64 kv
 constexpr int kOffVec = kOffDS + 2 * kTile;    // [2 stages] {lse2[128], D[128]} fp32
-constexpr int kOffBar = kOffVec + 2 * 1024;
+constexpr int kOffDQ = kOffVec + 2 * 1024;       // [2 stages][2 column halves] fp32 [128 q x 32]
+constexpr int kOffBar = kOffDQ + 4 * kTile;
 constexpr int kColST = 0, kColDPT = 256, kColDQ = 256, kColDV = 384, kColDK = 448;
 
 struct Bars {
@@ -98,7 +101,8 @@ enum : unsigned {
 
 __global__ void __launch_bounds__(kThreadsB, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO, const BParams p) {
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                  const __grid_constant__ CUtensorMap tmDQ, const BParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -129,6 +133,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
         tma_prefetch_desc(&tmDO);
+        tma_prefetch_desc(&tmDQ);
     }
     if (warp == kMmaWarp) {
         tmem_alloc(smem_addr(&bars->tmem_base), kTmemCols);
@@ -229,16 +234,25 @@ __global__ void __launch_bounds__(kThreadsB, 1)
                 tmem_wait_ld();
                 tc_fence_before();
                 mbar_arrive(smem_addr(&bars->dq_free));  // dP^T of the next tile may overwrite it
-                const int q_abs = i * 128 + row;
-                if (q_abs < p.n) {
-                    float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((size_t)bh * p.n + q_abs) * 64 + h * 32);
+                // Stage i % 2 was last read by the reduce of tile i - 2.
+                if (threadIdx.x == 0) tma_store_wait_read1();
+                named_bar_sync(1, kEwWarps * 32);
+                uint8_t* stage = smem + kOffDQ + (i & 1) * 2 * kTile + h * kTile;
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        atomicAdd(dst + c, make_float4(__uint_as_float(o[4 * c]), __uint_as_float(o[4 * c + 1]),
-                                                       __uint_as_float(o[4 * c + 2]), __uint_as_float(o[4 * c + 3])));
+                for (int c = 0; c < 8; ++c)  // 16-byte chunk c of the row at c ^ (row % 8): 128-byte swizzle
+                    *reinterpret_cast<uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4)) =
+                        make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                fence_proxy_async_smem();
+                named_bar_sync(1, kEwWarps * 32);
+                if (threadIdx.x == 0) {
+                    const uint32_t st0 = smem_addr(smem + kOffDQ + (i & 1) * 2 * kTile);
+                    tma_reduce_add_3d(&tmDQ, st0, 0, i * 128, bh);
+                    tma_reduce_add_3d(&tmDQ, st0 + kTile, 32, i * 128, bh);
+                    tma_store_commit();
                 }
             }
         }
+        if (threadIdx.x == 0) tma_store_wait0();  // the dQ reduces have completed
         if (ok) ok = warp_wait(smem_addr(&bars->acc_done), 0u, ctl, kSiteBEwDone);
         if (ok) {
             tc_fence_after();

@@ -949,6 +949,21 @@ int bf_bwd_launch(const BfBwdArgs* a) {
     if ((rc = make_map(&mk, a->k, a->bh, a->n)) != BF_OK) return rc;
     if ((rc = make_map(&mv, a->v, a->bh, a->n)) != BF_OK) return rc;
     if ((rc = make_map(&mdo, a->dout, a->bh, a->n)) != BF_OK) return rc;
+    // The fp32 dQ accumulator [BH][n][64] as a 3-D map for the kernel's TMA reduce-adds:
+    // 32-column (128-byte) x 128-row boxes with 128-byte swizzle; rows past n are clipped.
+    CUtensorMap mdq;
+    {
+        PFN_encodeTiled enc = get_encode_fn();
+        if (!enc) return bf_set_error(BF_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+        cuuint64_t dims[3] = {64, (cuuint64_t)a->n, (cuuint64_t)a->bh};
+        cuuint64_t strides[2] = {64 * 4, (cuuint64_t)a->n * 64 * 4};
+        cuuint32_t box[3] = {32, 128, 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        const CUresult r = enc(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_acc, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return bf_set_error(BF_ERR_CUDA, "cuTensorMapEncodeTiled rejected the dQ accumulator");
+    }
     static std::atomic<bool> done[64];  // per device; zero-initialised (static storage)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return bf_set_error(BF_ERR_CUDA, "cudaGetDevice failed");
@@ -987,7 +1002,7 @@ int bf_bwd_launch(const BfBwdArgs* a) {
     bp.dv = reinterpret_cast<__nv_bfloat16*>(a->dv);
     bp.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
     if ((rc = launch_err("backward prep kernel")) != BF_OK) return rc;
-    bfk::bwd::fa_bwd_kernel<<<(unsigned)blocks, bfk::bwd::kThreadsB, bfk::bwd::kSmemBytesB, stream>>>(mq, mk, mv, mdo, bp);
+    bfk::bwd::fa_bwd_kernel<<<(unsigned)blocks, bfk::bwd::kThreadsB, bfk::bwd::kSmemBytesB, stream>>>(mq, mk, mv, mdo, mdq, bp);
     {
         const cudaError_t le = cudaGetLastError();
         if (le != cudaSuccess) {

@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         const uint32_t tDPT = tmem + lane_off + kColDPT;
         const bool kv_ok = jt * 128 + row < p.n;
         uint8_t* ds_smem = smem + kOffDS + (row >> 6) * kTile;  // chunk holding this KV column
-        const int ds_unit = (row & 63) >> 3, ds_sub = (row & 7) * 2;
+        const int ds_unit = (row & 63) >> 3;
         bool ok = true;
         for (int i = 0; i < p.q_tiles && ok; ++i) {
             const uint32_t tST = tmem + lane_off + kColST + (uint32_t)(i & 1) * 128;
@@ -211,13 +211,17 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             // dS [q][kv] into shared memory, 128-byte swizzled K-major rows (A of dQ = dS K).
             // Earlier readers of this buffer (dQ(i-1) = dS(i-1) K) completed before this
             // thread observed dq_done(i-1).
+            // Lanes 2k and 2k+1 hold KV rows r and r+1 (r even): a 2x2 exchange gives the
+            // even lane query 2c and the odd lane query 2c+1 of both rows, one 4-byte store each.
+            {
+                const bool odd = lane & 1;
+                const int q_sub = (row & 6) * 2;  // byte offset of the row pair inside its 16-byte unit
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int q = h * 64 + 2 * c + e;
-                    const uint16_t v = (uint16_t)(e ? (dsk[c] >> 16) : (dsk[c] & 0xffffu));
-                    *reinterpret_cast<uint16_t*>(ds_smem + q * 128 + ((ds_unit ^ (q & 7)) << 4) + ds_sub) = v;
+                for (int c = 0; c < 32; ++c) {
+                    const uint32_t other = __shfl_xor_sync(0xffffffffu, dsk[c], 1);
+                    const uint32_t v = odd ? __byte_perm(other, dsk[c], 0x7632) : __byte_perm(dsk[c], other, 0x5410);
+                    const int q = h * 64 + 2 * c + (odd ? 1 : 0);
+                    *reinterpret_cast<uint32_t*>(ds_smem + q * 128 + ((ds_unit ^ (q & 7)) << 4) + q_sub) = v;
                 }
             }
             fence_proxy_async_smem();

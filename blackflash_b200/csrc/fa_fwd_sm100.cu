@@ -44,6 +44,7 @@
 #include <cuda_bf16.h>
 #include <math.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -760,11 +761,16 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, 
     cfg.blockDim = dim3(block);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
+    // BLACKFLASH_NO_PDL=1 launches with plain stream order (read once per process).
+    static const bool no_pdl = [] {
+        const char* v = getenv("BLACKFLASH_NO_PDL");
+        return v && v[0] && v[0] != '0';
+    }();
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = no_pdl ? 0 : 1;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

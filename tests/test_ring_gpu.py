@@ -104,12 +104,14 @@ def _ring_worker(rank, world, port, qkv, out, mode="ring"):
     if mode == "allgather":
         o = allgather_attention(*args)
     elif mode == "ipc":
-        # Two calls on the same ring context: the second (V negated) must not see the
-        # first call's blocks; O is linear in V.
+        # Two calls on the same ring context: the second must not see the first call's
+        # blocks. O is linear in V, so the first call (V negated) must give -O up to bf16
+        # rounding (the tensor core's accumulation is not exactly sign-symmetric); a stale
+        # block would differ by O(1).
         o2 = ipc_ring_attention(args[0], args[1], (-args[2]).contiguous(), 0.125)
         o = ipc_ring_attention(*args)
         torch.cuda.synchronize()
-        assert torch.equal(o2, -o), "second call on the ring saw stale data"
+        assert (o2.float() + o.float()).abs().max().item() <= 1e-2, "second call on the ring saw stale data"
         close_ipc_rings()
     else:
         o = ring_attention(*args, bidirectional=(mode == "ring"))

@@ -67,6 +67,10 @@ constexpr int kSoftWarps = 16;                       // 8 per query tile, 4 per 
 // With BF_REGSPLIT the block is 20 warps (a fourth, idle warp completes the last
 // warpgroup) so setmaxnreg can move registers from the issuer warps to the softmax.
 constexpr int kThreads = kSoftWarps * 32 + (BF_REGSPLIT ? 4 : 3) * 32;  // + TMA producer, S issuer, PV issuer
+#ifndef BF_SOFT_REGS
+#define BF_SOFT_REGS 104
+#endif
+constexpr int kSoftRegs = BF_SOFT_REGS, kIssueRegs = (96 * 640 - BF_SOFT_REGS * 512) / 128 / 8 * 8;
 constexpr int kTileBytes = kBM * kD * 2;  // 16 KiB (Q, K, V or O tile, bf16)
 constexpr int kTmemCols = 512;
 // TMEM columns: S_t at t*128; P_t (bf16, 64 columns) and O_t (fp32, 64 columns) after them.
@@ -262,11 +266,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
 #if BF_REGSPLIT
-    // Launch budget 96 x 640 = 61440: softmax 104 x 512 + issuers 64 x 128.
+    // Launch budget 96 x 640 = 61440 registers: softmax kSoftRegs x 512 + issuers kIssueRegs x 128.
+    static_assert(kSoftRegs * kSoftWarps * 32 + kIssueRegs * (kThreads - kSoftWarps * 32) <= 96 * kThreads,
+                  "register split exceeds the launch budget");
     if (warp < kSoftWarps)
-        regs_inc<104>();
+        regs_inc<kSoftRegs>();
     else
-        regs_dec<64>();
+        regs_dec<kIssueRegs>();
 #endif
     if (warp < kSoftWarps) {
         // ------------------------------------------------------------ softmax

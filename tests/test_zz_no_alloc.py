@@ -5,7 +5,7 @@ library instead of a caller workspace.
 
 Checked through the C ABI against blackflash_bwd (the entry point that takes a
 workspace) on two calls in a row, which also covers the second call finding the
-first call's data in the shared array. Tolerance as for the backward's parity
+first call's data in the shared array, and once against the double-precision oracle. Tolerance as for the backward's parity
 tests: max |err| <= 2e-2 * max |ref|, mean |err| <= 1e-2 * mean |ref|.
 This file sorts last so that a run stopping at its first failure has run the rest."""
 import pytest
@@ -46,6 +46,11 @@ def test_noalloc_backward_matches_workspace_backward():
         torch.cuda.synchronize()
         for name, g, r in zip(("dQ", "dK", "dV"), got, ref):
             _close(g, r, f"call {call}: {name}")
+        if call == 0:  # and, on its own, against the double-precision oracle
+            from oracle import oracle
+            exact = oracle.attn_bwd(q.cpu(), k.cpu(), v.cpu(), do.cpu(), 0.125)
+            for name, g, r in zip(("dQ", "dK", "dV"), got, exact):
+                _close(g, torch.from_numpy(r).cuda(), f"oracle: {name}")
 
 
 def test_noalloc_backward_rejects_oversize():

@@ -355,15 +355,20 @@ def run_ours(args, cfg_name):
         dist_mod.all_reduce(t, op=dist_mod.ReduceOp.MAX)
         return float(t.item())
 
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record(stream)
     for _ in range(args.warmup):
         step()
+    w1.record(stream)
     torch.cuda.synchronize()
+    warm_ms = max(w0.elapsed_time(w1) / args.warmup, 1e-3)
 
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    # keep the GPU loaded while the sampler settles
-    for _ in range(max(1, args.warmup)):
+    # Untimed steps that keep the GPU loaded while the sampler settles, for at least
+    # ~20 ms, so the timed steps start at the clocks of a busy GPU.
+    for _ in range(max(args.warmup, math.ceil(20.0 / warm_ms))):
         step()
     barrier()
     torch.cuda.synchronize()

@@ -231,8 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int t = 0; t < kQTiles; ++t) {
             mbar_init(smem_addr(&bars->s_full[t]), 1);
-            mbar_init(smem_addr(&bars->s_empty[t]), 2 * kBM);
-            mbar_init(smem_addr(&bars->p_full[t]), 2 * kBM);
+            mbar_init(smem_addr(&bars->s_empty[t]), 8);  // one arrival per softmax warp of the tile
+            mbar_init(smem_addr(&bars->p_full[t]), 8);
             mbar_init(smem_addr(&bars->pv_done[t]), 1);
         }
         mbar_init(smem_addr(&bars->drain), 1);
@@ -389,8 +389,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));  // the row's other half
                 };
 
+                // S_t is in registers (tcgen05.wait::ld is warp-wide): one lane tells the
+                // S issuer that it may be overwritten.
                 tc_fence_before();
-                mbar_arrive(bar_se);  // S_t is in registers: it may now be overwritten
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar_se);
                 const float mx = row_max();
                 m_raw = fmaxf(m_raw, mx);
                 const float m_new = mx * sl2;
@@ -426,7 +429,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_st16x32bx2_x16<32>(tP + 16, pk[1]);
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(bar_p);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar_p);
                 BF_TRACE(t, g, 6);
             }
             if (!ok) break;

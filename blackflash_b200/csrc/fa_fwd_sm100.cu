@@ -59,7 +59,10 @@ constexpr int kD = 64;          // head dimension
 constexpr int kBM = 128;        // query rows per tile
 constexpr int kBN = 128;        // KV rows per tile
 constexpr int kQTiles = 2;      // query tiles per work item
-constexpr int kStages = 3;      // K/V ring depth
+#ifndef BF_KV_STAGES
+#define BF_KV_STAGES 3
+#endif
+constexpr int kStages = BF_KV_STAGES;  // K/V ring depth
 constexpr int kSoftWarps = 16;                       // 8 per query tile, 4 per scheduler
 #ifndef BF_REGSPLIT
 #define BF_REGSPLIT 1

@@ -162,6 +162,36 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         const bool kv_ok = jt * 128 + row < p.n;
         uint8_t* ds_smem = smem + kOffDS + (row >> 6) * kTile;  // chunk holding this KV column
         const int ds_unit = (row & 63) >> 3;
+        // dQ_k (rows = queries): read it out of TMEM (which lets dP^T of tile k+1 be
+        // computed there), stage it and add it to the fp32 accumulator by TMA.
+        auto drain_dq = [&](int k) -> bool {
+            if (!(warp_wait(smem_addr(&bars->dq_done), (uint32_t)k & 1u, ctl, kSiteBEwDone))) return false;
+            tc_fence_after();
+            {
+                uint32_t o[32];
+                tmem_ld16x32bx2_x32<32>(tmem + lane_off + kColDQ, o);
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(smem_addr(&bars->dq_free));  // dP^T of the next tile may overwrite it
+                // Stage k % 2 was last read by the reduce of tile k - 2.
+                if (threadIdx.x == 0) tma_store_wait_read1();
+                named_bar_sync(1, kEwWarps * 32);
+                uint8_t* stage = smem + kOffDQ + (k & 1) * 2 * kTile + h * kTile;
+#pragma unroll
+                for (int c = 0; c < 8; ++c)  // 16-byte chunk c of the row at c ^ (row % 8): 128-byte swizzle
+                    *reinterpret_cast<uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4)) =
+                        make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                fence_proxy_async_smem();
+                named_bar_sync(1, kEwWarps * 32);
+                if (threadIdx.x == 0) {
+                    const uint32_t st0 = smem_addr(smem + kOffDQ + (k & 1) * 2 * kTile);
+                    tma_reduce_add_3d(&tmDQ, st0, 0, k * 128, bh);
+                    tma_reduce_add_3d(&tmDQ, st0 + kTile, 32, k * 128, bh);
+                    tma_store_commit();
+                }
+            }
+            return true;
+        };
         bool ok = true;
         for (int i = 0; i < p.q_tiles && ok; ++i) {
             const uint32_t tST = tmem + lane_off + kColST + (uint32_t)(i & 1) * 128;
@@ -188,6 +218,9 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             tmem_st16x32bx2_x16<32>(tST, pk);
             tmem_st16x32bx2_x16<32>(tST + 16, pk + 16);
 
+            // dQ of the previous tile: its product ran while this tile's P was computed.
+            if (i > 0 && !(ok = drain_dq(i - 1))) break;
+
             // dS = P (dP - D), from the bf16 P the dV product uses (dS is rounded to bf16 too).
             if (!(ok = warp_wait(smem_addr(&bars->dp_full), (uint32_t)i & 1u, ctl, kSiteBEwS))) break;
             tc_fence_after();
@@ -210,7 +243,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             }
             // dS [q][kv] into shared memory, 128-byte swizzled K-major rows (A of dQ = dS K).
             // Earlier readers of this buffer (dQ(i-1) = dS(i-1) K) completed before this
-            // thread observed dq_done(i-1).
+            // thread observed dq_done(i-1) in drain_dq(i - 1).
             // Lanes 2k and 2k+1 hold KV rows r and r+1 (r even): a 2x2 exchange gives the
             // even lane query 2c and the odd lane query 2c+1 of both rows, one 4-byte store each.
             {
@@ -229,33 +262,8 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             tc_fence_before();
             mbar_arrive(smem_addr(&bars->p_ready));
 
-            // dQ_i (rows = queries) into the fp32 accumulator.
-            if (!(ok = warp_wait(smem_addr(&bars->dq_done), (uint32_t)i & 1u, ctl, kSiteBEwDone))) break;
-            tc_fence_after();
-            {
-                uint32_t o[32];
-                tmem_ld16x32bx2_x32<32>(tmem + lane_off + kColDQ, o);
-                tmem_wait_ld();
-                tc_fence_before();
-                mbar_arrive(smem_addr(&bars->dq_free));  // dP^T of the next tile may overwrite it
-                // Stage i % 2 was last read by the reduce of tile i - 2.
-                if (threadIdx.x == 0) tma_store_wait_read1();
-                named_bar_sync(1, kEwWarps * 32);
-                uint8_t* stage = smem + kOffDQ + (i & 1) * 2 * kTile + h * kTile;
-#pragma unroll
-                for (int c = 0; c < 8; ++c)  // 16-byte chunk c of the row at c ^ (row % 8): 128-byte swizzle
-                    *reinterpret_cast<uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4)) =
-                        make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-                fence_proxy_async_smem();
-                named_bar_sync(1, kEwWarps * 32);
-                if (threadIdx.x == 0) {
-                    const uint32_t st0 = smem_addr(smem + kOffDQ + (i & 1) * 2 * kTile);
-                    tma_reduce_add_3d(&tmDQ, st0, 0, i * 128, bh);
-                    tma_reduce_add_3d(&tmDQ, st0 + kTile, 32, i * 128, bh);
-                    tma_store_commit();
-                }
-            }
         }
+        if (ok) ok = drain_dq(p.q_tiles - 1);
         if (threadIdx.x == 0) tma_store_wait0();  // the dQ reduces have completed
         if (ok) ok = warp_wait(smem_addr(&bars->acc_done), 0u, ctl, kSiteBEwDone);
         if (ok) {

@@ -222,3 +222,33 @@ def test_build_tracks_every_source_and_header():
     present = {os.path.basename(f) for f in glob.glob(os.path.join(build.CSRC, "*"))
                if f.endswith((".cu", ".cuh", ".h"))}
     assert present <= listed, sorted(present - listed)
+
+
+def test_ring_entry_points_reject_bad_arguments_without_device_work():
+    """blackflash_ring_* check their arguments before any CUDA call (csrc/ring_ipc.cu)."""
+    import ctypes
+
+    from blackflash_b200 import _lib
+    lib = _lib.load()
+    assert lib.blackflash_ring_handle_bytes() == 64
+    ring = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    for world, rank, bh, n, d in [(1, 0, 4, 128, 64), (4, 4, 4, 128, 64), (4, 0, 0, 128, 64), (4, 0, 4, 100, 64),
+                                  (4, 0, 4, 128, 128)]:
+        rc = lib.blackflash_ring_create(world, rank, bh, n, d, ctypes.byref(ring), handle)
+        assert rc == _lib.BF_ERR_ARG, (world, rank, bh, n, d)
+        assert lib.blackflash_last_error()
+    assert lib.blackflash_ring_connect(None, handle) == _lib.BF_ERR_ARG
+    assert lib.blackflash_ring_forward(None, 16, 16, 16, 16, None, 0.125, None) == _lib.BF_ERR_ARG
+    assert lib.blackflash_ring_destroy(None) == _lib.BF_OK
+
+
+def test_bidirectional_schedule_covers_every_block_once():
+    from blackflash_b200.ring import bidirectional_schedule
+    for world in range(1, 9):
+        for rank in range(world):
+            steps = bidirectional_schedule(world, rank)
+            assert steps[0] == [rank]
+            blocks = [b for st in steps for b in st]
+            assert sorted(blocks) == list(range(world))
+            assert len(steps) == world // 2 + 1
